@@ -1,0 +1,277 @@
+// fa_api.cu -- extern "C" entry points of libfa_sm100.so (see include/fa_sm100.h).
+//
+// Host half of the boundary that replaces, in the reference:
+//   csrc/flash_api.cpp:14-29   input checks        -> fa_sm100_check_params
+//   csrc/flash_api.cpp:33-65   parameter marshalling + launch
+//   csrc/flash_fwd_launch.cu:8-31 dtype/head_dim dispatch + grid
+// The launcher encodes one TMA descriptor per operand (Q, K, V), picks the
+// kernel instantiation <head_dim, bf16, causal> and launches it on the given
+// stream.  Nothing is allocated per call.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "fa_fwd_sm100.cuh"
+#include "fa_lse_merge.cuh"
+#include "fa_sm100.h"
+
+namespace {
+
+// Library-owned error flag used when the caller passes none.  Device code
+// writes it on a bounded-wait timeout; fa_sm100_take_device_error reads it.
+__device__ int32_t g_fa_error_flag;
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  std::once_flag once;
+  int sm_major = 0;
+  int num_sms = 0;
+  int32_t* error_flag = nullptr;  // device address of g_fa_error_flag
+  int status = FA_OK;
+};
+DeviceState g_dev[kMaxDevices];
+
+int device_state(int dev, DeviceState** out) {
+  if (dev < 0 || dev >= kMaxDevices) return FA_ERR_INVALID_ARG;
+  DeviceState& s = g_dev[dev];
+  std::call_once(s.once, [&] {
+    if (cudaDeviceGetAttribute(&s.sm_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      s.status = FA_ERR_CUDA;
+      return;
+    }
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_fa_error_flag) != cudaSuccess) {
+      s.status = FA_ERR_CUDA;
+      return;
+    }
+    s.error_flag = static_cast<int32_t*>(addr);
+  });
+  *out = &s;
+  return s.status;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+// TMA descriptor over a BSHD operand viewed as 4-D (d, head, seq, batch) with
+// a (64, 1, 128, 1) box and 128-byte swizzle: one box is 128 rows of 128
+// bytes, exactly the canonical K-major / MN-major SW128 UMMA atom stack.
+int encode_operand(CUtensorMap* m, const void* base, bool bf16, int head_dim, int64_t seqlen,
+                   int64_t heads, int64_t batch, int64_t row_stride, int64_t head_stride,
+                   int64_t batch_stride) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return FA_ERR_CUDA;
+  // Strides of extent-1 dimensions never matter; give them a legal value.
+  int64_t hs = heads > 1 ? head_stride : head_dim;
+  int64_t rs = seqlen > 1 ? row_stride : heads * head_dim;
+  int64_t bs = batch > 1 ? batch_stride : seqlen * heads * head_dim;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(seqlen), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(hs * 2), static_cast<cuuint64_t>(rs * 2),
+                           static_cast<cuuint64_t>(bs * 2)};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(fa::kBlockM), 1};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_ERR_UNSUPPORTED;
+}
+
+// Bound on any single device-side wait.  FA_SM100_TIMEOUT_MS overrides the
+// 2 s default (read once per process).
+uint64_t timeout_ns() {
+  static const uint64_t ns = [] {
+    const char* e = std::getenv("FA_SM100_TIMEOUT_MS");
+    const long ms = e != nullptr ? std::strtol(e, nullptr, 10) : 0;
+    return static_cast<uint64_t>(ms > 0 ? ms : 2000) * 1000ull * 1000ull;
+  }();
+  return ns;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+bool stride_ok(int64_t s) { return s >= 0 && (s % 8) == 0; }  // 16 bytes of 16-bit elements
+
+template <int D, bool BF16, bool CAUSAL>
+int launch(const fa::FwdKernelParams& kp, cudaStream_t stream) {
+  using Tr = fa::FwdTraits<D>;
+  auto kernel = fa::fa_fwd_sm100_kernel<D, BF16, CAUSAL>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  if (e != cudaSuccess) return FA_ERR_CUDA;
+  const int64_t grid = static_cast<int64_t>(kp.num_m_blocks) * kp.heads * kp.batch;
+  if (grid <= 0 || grid > 0x7fffffffLL) return FA_ERR_UNSUPPORTED;
+  kernel<<<static_cast<unsigned>(grid), fa::kThreads, Tr::kSmemBytes, stream>>>(kp);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? FA_OK : FA_ERR_CUDA;
+}
+
+template <int D, bool BF16>
+int launch_causal(const fa::FwdKernelParams& kp, bool causal, cudaStream_t s) {
+  return causal ? launch<D, BF16, true>(kp, s) : launch<D, BF16, false>(kp, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_sm100_check_params(const FaParams* p) {
+  if (p == nullptr) return FA_ERR_INVALID_ARG;
+  if (p->batch < 0 || p->seqlen_q < 0 || p->seqlen_k < 0 || p->heads <= 0 || p->heads_k <= 0) {
+    return FA_ERR_INVALID_ARG;
+  }
+  if (p->head_dim != 64 && p->head_dim != 128) return FA_ERR_UNSUPPORTED;
+  if (p->heads_k != p->heads) return FA_ERR_UNSUPPORTED;
+  if (!std::isfinite(p->softmax_scale)) return FA_ERR_INVALID_ARG;
+  if (p->batch == 0 || p->seqlen_q == 0) return FA_OK;  // nothing to compute
+  if (p->q == nullptr || p->o == nullptr) return FA_ERR_INVALID_ARG;
+  if (p->seqlen_k > 0 && (p->k == nullptr || p->v == nullptr)) return FA_ERR_INVALID_ARG;
+  if (!aligned16(p->q) || !aligned16(p->o) || (p->seqlen_k > 0 && (!aligned16(p->k) || !aligned16(p->v)))) {
+    return FA_ERR_ALIGNMENT;
+  }
+  const int64_t st[] = {p->q_batch_stride, p->q_row_stride, p->q_head_stride, p->k_batch_stride,
+                        p->k_row_stride,   p->k_head_stride, p->v_batch_stride, p->v_row_stride,
+                        p->v_head_stride,  p->o_batch_stride, p->o_row_stride, p->o_head_stride};
+  for (int64_t s : st) {
+    if (!stride_ok(s)) return FA_ERR_ALIGNMENT;
+  }
+  if (p->lse != nullptr && (reinterpret_cast<uintptr_t>(p->lse) & 3u) != 0) return FA_ERR_ALIGNMENT;
+  if (p->lse != nullptr && (p->lse_batch_stride < 0 || p->lse_head_stride < 0)) return FA_ERR_INVALID_ARG;
+  return FA_OK;
+}
+
+int fa_sm100_fwd(const FaParams* p, void* stream_ptr) {
+  int rc = fa_sm100_check_params(p);
+  if (rc != FA_OK) return rc;
+  if (p->batch == 0 || p->seqlen_q == 0) return FA_OK;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  DeviceState* ds = nullptr;
+  rc = device_state(dev, &ds);
+  if (rc != FA_OK) return rc;
+  if (ds->sm_major != 10) return FA_ERR_NO_DEVICE;
+
+  const bool bf16 = p->is_bf16 != 0;
+  fa::FwdKernelParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  rc = encode_operand(&kp.tm_q, p->q, bf16, p->head_dim, p->seqlen_q, p->heads, p->batch, p->q_row_stride,
+                      p->q_head_stride, p->q_batch_stride);
+  if (rc != FA_OK) return rc;
+  if (p->seqlen_k > 0) {
+    rc = encode_operand(&kp.tm_k, p->k, bf16, p->head_dim, p->seqlen_k, p->heads_k, p->batch,
+                        p->k_row_stride, p->k_head_stride, p->k_batch_stride);
+    if (rc != FA_OK) return rc;
+    rc = encode_operand(&kp.tm_v, p->v, bf16, p->head_dim, p->seqlen_k, p->heads_k, p->batch,
+                        p->v_row_stride, p->v_head_stride, p->v_batch_stride);
+    if (rc != FA_OK) return rc;
+  }
+  kp.o = p->o;
+  kp.lse = p->lse;
+  kp.error_flag = p->error_flag != nullptr ? p->error_flag : ds->error_flag;
+  kp.o_batch_stride = p->o_batch_stride;
+  kp.o_row_stride = p->o_row_stride;
+  kp.o_head_stride = p->o_head_stride;
+  kp.lse_batch_stride = p->lse_batch_stride;
+  kp.lse_head_stride = p->lse_head_stride;
+  kp.q_pos_offset = p->q_pos_offset;
+  kp.k_pos_offset = p->k_pos_offset;
+  kp.timeout_ns = timeout_ns();
+  kp.seqlen_q = p->seqlen_q;
+  kp.seqlen_k = p->seqlen_k;
+  kp.heads = p->heads;
+  kp.batch = p->batch;
+  kp.num_m_blocks = (p->seqlen_q + 2 * fa::kBlockM - 1) / (2 * fa::kBlockM);
+  kp.scale = p->softmax_scale;
+  kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream_ptr);
+  const bool causal = p->is_causal != 0;
+  if (p->head_dim == 64) {
+    return bf16 ? launch_causal<64, true>(kp, causal, s) : launch_causal<64, false>(kp, causal, s);
+  }
+  return bf16 ? launch_causal<128, true>(kp, causal, s) : launch_causal<128, false>(kp, causal, s);
+}
+
+int fa_sm100_lse_merge(const float* const* o_parts, const float* const* lse_parts, int32_t n_parts,
+                       int32_t rows, int32_t heads, int32_t head_dim, void* o_out, int64_t o_row_stride,
+                       int64_t o_head_stride, int32_t out_is_bf16, float* lse_out, void* stream_ptr) {
+  if (o_parts == nullptr || lse_parts == nullptr || o_out == nullptr) return FA_ERR_INVALID_ARG;
+  if (n_parts < 1 || n_parts > fa::kMaxMergeParts || rows < 0 || heads <= 0) return FA_ERR_INVALID_ARG;
+  if (head_dim != 64 && head_dim != 128) return FA_ERR_UNSUPPORTED;
+  if (rows == 0) return FA_OK;
+  fa::MergeParams mp;
+  std::memset(&mp, 0, sizeof(mp));
+  for (int i = 0; i < n_parts; ++i) {
+    if (o_parts[i] == nullptr || lse_parts[i] == nullptr) return FA_ERR_INVALID_ARG;
+    mp.o_parts[i] = o_parts[i];
+    mp.lse_parts[i] = lse_parts[i];
+  }
+  mp.n_parts = n_parts;
+  mp.rows = rows;
+  mp.heads = heads;
+  mp.o_out = o_out;
+  mp.o_row_stride = o_row_stride;
+  mp.o_head_stride = o_head_stride;
+  mp.lse_out = lse_out;
+  return fa::launch_lse_merge(mp, head_dim, out_is_bf16 != 0, static_cast<cudaStream_t>(stream_ptr));
+}
+
+int fa_sm100_take_device_error(int device) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return FA_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return FA_ERR_CUDA;
+  int32_t v = 0;
+  int rc = FA_OK;
+  if (cudaMemcpyFromSymbol(&v, g_fa_error_flag, sizeof(v)) != cudaSuccess) {
+    rc = FA_ERR_CUDA;
+  } else {
+    const int32_t zero = 0;
+    if (cudaMemcpyToSymbol(g_fa_error_flag, &zero, sizeof(zero)) != cudaSuccess) rc = FA_ERR_CUDA;
+    if (rc == FA_OK) rc = v;
+  }
+  if (device != prev) cudaSetDevice(prev);
+  return rc;
+}
+
+const char* fa_sm100_status_string(int status) {
+  switch (status) {
+    case FA_OK: return "ok";
+    case FA_ERR_INVALID_ARG: return "invalid argument";
+    case FA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim must be 64 or 128, heads_k == heads, strides TMA-encodable)";
+    case FA_ERR_ALIGNMENT: return "pointers must be 16-byte aligned and strides multiples of 8 elements";
+    case FA_ERR_CUDA: return "CUDA error";
+    case FA_ERR_NO_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case FA_ERR_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int fa_sm100_params_size(void) { return static_cast<int>(sizeof(FaParams)); }
+
+int fa_sm100_num_sms(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  return n;
+}
+
+}  // extern "C"

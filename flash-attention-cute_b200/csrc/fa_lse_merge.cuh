@@ -1,0 +1,89 @@
+// fa_lse_merge.cuh -- combine partial attention results computed over
+// disjoint key sets for the same query rows.
+//
+// For each (row, head):  lse = log(sum_i exp(lse_i));  O = sum_i exp(lse_i - lse) O_i.
+// Partial O_i are fp32 (rows, heads, head_dim) contiguous, partial LSE_i are
+// fp32 (heads, rows).  A part whose LSE is -inf (no visible key) contributes
+// nothing; if every part is -inf the row's O is 0 and its LSE -inf.  This is
+// the merge that sequence-sharded (context-parallel) runs need when a rank
+// computes its rows against key chunks one at a time.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <type_traits>
+
+namespace fa {
+
+constexpr int kMaxMergeParts = 16;
+
+struct MergeParams {
+  const float* o_parts[kMaxMergeParts];
+  const float* lse_parts[kMaxMergeParts];
+  void* o_out;
+  float* lse_out;
+  int64_t o_row_stride, o_head_stride;
+  int n_parts, rows, heads;
+};
+
+// One warp per (row, head); each lane owns D/32 consecutive elements.
+template <int D, bool kBf16>
+__global__ void __launch_bounds__(256) fa_lse_merge_kernel(const __grid_constant__ MergeParams p) {
+  const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_id >= static_cast<int64_t>(p.rows) * p.heads) return;
+  const int row = static_cast<int>(warp_id / p.heads);
+  const int head = static_cast<int>(warp_id % p.heads);
+  float mx = -INFINITY;
+  for (int i = 0; i < p.n_parts; ++i) mx = fmaxf(mx, p.lse_parts[i][static_cast<int64_t>(head) * p.rows + row]);
+  constexpr int E = D / 32;
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  float denom = 0.f;
+  if (mx != -INFINITY) {
+    for (int i = 0; i < p.n_parts; ++i) {
+      const float li = p.lse_parts[i][static_cast<int64_t>(head) * p.rows + row];
+      const float w = __expf(li - mx);
+      denom += w;
+      const float* src = p.o_parts[i] + (static_cast<int64_t>(row) * p.heads + head) * D + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = fmaf(w, src[e], acc[e]);
+    }
+  }
+  const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  T* dst = reinterpret_cast<T*>(p.o_out) + static_cast<int64_t>(row) * p.o_row_stride +
+           static_cast<int64_t>(head) * p.o_head_stride + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    if constexpr (kBf16) {
+      dst[e] = __float2bfloat16_rn(acc[e] * inv);
+    } else {
+      dst[e] = __float2half_rn(acc[e] * inv);
+    }
+  }
+  if (lane == 0 && p.lse_out != nullptr) {
+    p.lse_out[static_cast<int64_t>(head) * p.rows + row] = denom > 0.f ? mx + logf(denom) : -INFINITY;
+  }
+}
+
+inline int launch_lse_merge(const MergeParams& mp, int head_dim, bool bf16, cudaStream_t stream) {
+  const int64_t warps = static_cast<int64_t>(mp.rows) * mp.heads;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > 0x7fffffffLL) return -2;
+  const unsigned g = static_cast<unsigned>(blocks);
+  if (head_dim == 64) {
+    if (bf16) fa_lse_merge_kernel<64, true><<<g, 256, 0, stream>>>(mp);
+    else fa_lse_merge_kernel<64, false><<<g, 256, 0, stream>>>(mp);
+  } else {
+    if (bf16) fa_lse_merge_kernel<128, true><<<g, 256, 0, stream>>>(mp);
+    else fa_lse_merge_kernel<128, false><<<g, 256, 0, stream>>>(mp);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace fa

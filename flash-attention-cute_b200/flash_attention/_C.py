@@ -1,0 +1,249 @@
+"""Binding of libfa_sm100.so -- the stand-in for the reference's compiled
+``flash_attention._C`` module (pybind11, csrc/flash_api.cpp:70-72).
+
+``forward(q, k, v, causal)`` keeps the reference signature and error
+behaviour: the same input checks with the same messages raised as
+``RuntimeError`` (csrc/flash_api.cpp:14-29), output allocated with
+``torch.empty_like(q)`` (flash_api.cpp:31), softmax scale ``1/sqrt(d)``
+(flash_api.cpp:59-60), launched on the current stream of q's device
+(flash_api.cpp:64; a device guard is added).  The native call goes through
+the C ABI declared in ``include/fa_sm100.h`` via ctypes; there is no CPU
+path: if the library is missing, importing this module fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libfa_sm100.so")
+
+FA_OK = 0
+
+
+class FaParams(ctypes.Structure):
+    """Mirror of ``struct FaParams`` in include/fa_sm100.h."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("seqlen_q", ctypes.c_int32),
+        ("seqlen_k", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("heads_k", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("q_batch_stride", ctypes.c_int64),
+        ("q_row_stride", ctypes.c_int64),
+        ("q_head_stride", ctypes.c_int64),
+        ("k_batch_stride", ctypes.c_int64),
+        ("k_row_stride", ctypes.c_int64),
+        ("k_head_stride", ctypes.c_int64),
+        ("v_batch_stride", ctypes.c_int64),
+        ("v_row_stride", ctypes.c_int64),
+        ("v_head_stride", ctypes.c_int64),
+        ("o_batch_stride", ctypes.c_int64),
+        ("o_row_stride", ctypes.c_int64),
+        ("o_head_stride", ctypes.c_int64),
+        ("lse_batch_stride", ctypes.c_int64),
+        ("lse_head_stride", ctypes.c_int64),
+        ("softmax_scale", ctypes.c_float),
+        ("is_causal", ctypes.c_int32),
+        ("is_bf16", ctypes.c_int32),
+        ("q_pos_offset", ctypes.c_int64),
+        ("k_pos_offset", ctypes.c_int64),
+        ("error_flag", ctypes.c_void_p),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(_LIB_PATH):
+        raise ImportError(
+            f"{_LIB_PATH} is missing: build it with `python flash-attention-cute_b200/build_ext.py` "
+            "(there is no fallback implementation)"
+        )
+    lib = ctypes.CDLL(_LIB_PATH)
+    lib.fa_sm100_check_params.argtypes = [ctypes.POINTER(FaParams)]
+    lib.fa_sm100_check_params.restype = ctypes.c_int
+    lib.fa_sm100_fwd.argtypes = [ctypes.POINTER(FaParams), ctypes.c_void_p]
+    lib.fa_sm100_fwd.restype = ctypes.c_int
+    lib.fa_sm100_lse_merge.argtypes = [
+        ctypes.POINTER(ctypes.c_void_p),
+        ctypes.POINTER(ctypes.c_void_p),
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_int32,
+        ctypes.c_void_p,
+        ctypes.c_int64,
+        ctypes.c_int64,
+        ctypes.c_int32,
+        ctypes.c_void_p,
+        ctypes.c_void_p,
+    ]
+    lib.fa_sm100_lse_merge.restype = ctypes.c_int
+    lib.fa_sm100_take_device_error.argtypes = [ctypes.c_int]
+    lib.fa_sm100_take_device_error.restype = ctypes.c_int
+    lib.fa_sm100_status_string.argtypes = [ctypes.c_int]
+    lib.fa_sm100_status_string.restype = ctypes.c_char_p
+    lib.fa_sm100_num_sms.argtypes = [ctypes.c_int]
+    lib.fa_sm100_num_sms.restype = ctypes.c_int
+    lib.fa_sm100_params_size.argtypes = []
+    lib.fa_sm100_params_size.restype = ctypes.c_int
+    if lib.fa_sm100_params_size() != ctypes.sizeof(FaParams):
+        raise ImportError(
+            f"FaParams layout mismatch: library {lib.fa_sm100_params_size()} bytes, "
+            f"binding {ctypes.sizeof(FaParams)} bytes"
+        )
+    return lib
+
+
+lib = _load()
+
+
+def status_string(rc: int) -> str:
+    return lib.fa_sm100_status_string(rc).decode()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != FA_OK:
+        raise RuntimeError(f"{what} failed: {status_string(rc)} (status {rc})")
+
+
+def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    # Same checks and messages as csrc/flash_api.cpp:14-29 ...
+    if not q.is_cuda:
+        raise RuntimeError("q must be on CUDA")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("q must be fp16 or bf16")
+    if q.stride(-1) != 1:
+        raise RuntimeError("q must be contiguous in last dim")
+    if k.stride(-1) != 1:
+        raise RuntimeError("k must be contiguous in last dim")
+    if v.stride(-1) != 1:
+        raise RuntimeError("v must be contiguous in last dim")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise RuntimeError("q, k, v must be 4-D (batch, seqlen, heads, head_dim)")
+    head_dim = q.size(3)
+    if head_dim not in (64, 128):
+        raise RuntimeError("head_dim must be 64 or 128")
+    if q.size(2) % k.size(2) != 0:
+        raise RuntimeError("heads must be divisible by heads_k (for GQA)")
+    # ... plus the ones the reference leaves out (its kernel would read K/V
+    # of the wrong type, device or head otherwise).
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise RuntimeError("q, k and v must have the same dtype")
+    if k.device != q.device or v.device != q.device:
+        raise RuntimeError("q, k and v must be on the same device")
+    if k.size(2) != q.size(2):
+        raise RuntimeError("heads_k must equal heads (GQA/MQA is not supported by this kernel)")
+    if k.shape != v.shape or k.size(0) != q.size(0) or k.size(3) != head_dim:
+        raise RuntimeError("k and v must be (batch, seqlen_k, heads, head_dim) matching q")
+
+
+def fill_params(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    o: torch.Tensor,
+    lse: torch.Tensor | None,
+    causal: bool,
+    softmax_scale: float | None = None,
+    q_pos_offset: int = 0,
+    k_pos_offset: int = 0,
+) -> FaParams:
+    p = FaParams()
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    p.batch, p.seqlen_q, p.heads, p.head_dim = q.shape
+    p.seqlen_k, p.heads_k = k.size(1), k.size(2)
+    p.q_batch_stride, p.q_row_stride, p.q_head_stride = q.stride(0), q.stride(1), q.stride(2)
+    p.k_batch_stride, p.k_row_stride, p.k_head_stride = k.stride(0), k.stride(1), k.stride(2)
+    p.v_batch_stride, p.v_row_stride, p.v_head_stride = v.stride(0), v.stride(1), v.stride(2)
+    p.o_batch_stride, p.o_row_stride, p.o_head_stride = o.stride(0), o.stride(1), o.stride(2)
+    if lse is not None:
+        p.lse_batch_stride, p.lse_head_stride = lse.stride(0), lse.stride(1)
+    p.softmax_scale = (1.0 / math.sqrt(q.size(3))) if softmax_scale is None else float(softmax_scale)
+    p.is_causal = 1 if causal else 0
+    p.is_bf16 = 1 if q.dtype == torch.bfloat16 else 0
+    p.q_pos_offset = int(q_pos_offset)
+    p.k_pos_offset = int(k_pos_offset)
+    p.error_flag = None
+    return p
+
+
+def launch(p: FaParams, device: torch.device) -> None:
+    """Enqueue the kernel for filled params on the current stream of `device`."""
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _check(lib.fa_sm100_fwd(ctypes.byref(p), ctypes.c_void_p(stream)), "fa_sm100_fwd")
+
+
+def forward_with_lse(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    causal: bool = False,
+    *,
+    softmax_scale: float | None = None,
+    q_pos_offset: int = 0,
+    k_pos_offset: int = 0,
+    want_lse: bool = True,
+    out: torch.Tensor | None = None,
+    lse_out: torch.Tensor | None = None,
+):
+    _validate(q, k, v)
+    o = torch.empty_like(q) if out is None else out
+    lse = None
+    if want_lse:
+        lse = (
+            torch.empty((q.size(0), q.size(2), q.size(1)), dtype=torch.float32, device=q.device)
+            if lse_out is None
+            else lse_out
+        )
+    p = fill_params(q, k, v, o, lse, causal, softmax_scale, q_pos_offset, k_pos_offset)
+    launch(p, q.device)
+    return o, lse
+
+
+def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool) -> torch.Tensor:
+    """``flash_attention._C.forward(q, k, v, causal) -> o`` (csrc/flash_api.cpp:9-68)."""
+    o, _ = forward_with_lse(q, k, v, causal, want_lse=False)
+    return o
+
+
+def lse_merge(o_parts, lse_parts, o_out: torch.Tensor, lse_out: torch.Tensor | None = None) -> None:
+    """Merge fp32 partials (rows, heads, d) / (heads, rows) into o_out (rows, heads, d)."""
+    n = len(o_parts)
+    rows, heads, d = o_parts[0].shape
+    for t in list(o_parts) + list(lse_parts):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.device != o_out.device:
+            raise RuntimeError("partials must be contiguous fp32 tensors on the output's device")
+    arr_o = (ctypes.c_void_p * n)(*[t.data_ptr() for t in o_parts])
+    arr_l = (ctypes.c_void_p * n)(*[t.data_ptr() for t in lse_parts])
+    with torch.cuda.device(o_out.device):
+        stream = torch.cuda.current_stream(o_out.device).cuda_stream
+        rc = lib.fa_sm100_lse_merge(
+            arr_o,
+            arr_l,
+            n,
+            rows,
+            heads,
+            d,
+            o_out.data_ptr(),
+            o_out.stride(0),
+            o_out.stride(1),
+            1 if o_out.dtype == torch.bfloat16 else 0,
+            lse_out.data_ptr() if lse_out is not None else None,
+            ctypes.c_void_p(stream),
+        )
+    _check(rc, "fa_sm100_lse_merge")
+
+
+def take_device_error(device_index: int) -> int:
+    return lib.fa_sm100_take_device_error(int(device_index))

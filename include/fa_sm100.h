@@ -1,0 +1,128 @@
+/*
+ * fa_sm100.h -- C ABI of the B200 (sm_100a) attention forward.
+ *
+ * This is the drop-in boundary for the attention-forward path of
+ * flash-attention-cute.  Plain pointers, sizes and strides only: no torch or
+ * C++ types cross it, so ctypes / cffi / any FFI can bind it directly.
+ *
+ * Reference interfaces replaced (paths inside the flash-attention-cute tree):
+ *   struct FaParams          <- flash::ForwardParams           csrc/flash.h:6-45
+ *   fa_sm100_fwd()           <- flash::run_flash_attention_forward
+ *                                                               csrc/flash_fwd_launch.cu:25-31
+ *                               (declared csrc/flash_api.cpp:5-7, called :65)
+ *   fa_sm100_check_params()  <- the TORCH_CHECKs of flash_attn_forward
+ *                                                               csrc/flash_api.cpp:14-29
+ *   fa_sm100_lse_merge()     <- no reference counterpart; merges partial
+ *                               (O, LSE) pairs for sequence-sharded runs
+ *
+ * Semantics (identical to the reference kernel csrc/flash_fwd_kernel.cuh):
+ *   O[b,i,h,:] = sum_j softmax_j(scale * Q[b,i,h,:] . K[b,j,h,:]) V[b,j,h,:]
+ *   causal masks key j > query i (top-left aligned, kernel.cuh:174-188),
+ *   a row whose softmax sum is 0 produces O = 0 (kernel.cuh:277).
+ * Additions over the reference: LSE[b,h,i] = logsumexp_j(scale * q_i . k_j)
+ * in natural log (fp32), sequence tails (any seqlen >= 1), an int status
+ * instead of a silent launch, and global query/key position offsets used by
+ * context-parallel sharding.
+ */
+#ifndef FA_SM100_H_
+#define FA_SM100_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+#define FA_OK                    0
+#define FA_ERR_INVALID_ARG      -1  /* null pointer, negative size, ...          */
+#define FA_ERR_UNSUPPORTED      -2  /* head_dim not 64/128, heads_k != heads ... */
+#define FA_ERR_ALIGNMENT        -3  /* base pointer or stride not 16-byte aligned */
+#define FA_ERR_CUDA             -4  /* a CUDA runtime/driver call failed          */
+#define FA_ERR_NO_DEVICE        -5  /* current device is not an sm_100 part       */
+#define FA_ERR_TIMEOUT          -6  /* a bounded device wait ran out (see below)  */
+
+/* Launch parameters.  Strides are in ELEMENTS (not bytes), like
+ * flash::ForwardParams (csrc/flash.h:21-36).  Layout is BSHD:
+ * q[b, s, h, d] lives at q + b*q_batch_stride + s*q_row_stride + h*q_head_stride + d. */
+typedef struct FaParams {
+    const void *q;          /* (batch, seqlen_q, heads,   head_dim) fp16/bf16 */
+    const void *k;          /* (batch, seqlen_k, heads_k, head_dim)           */
+    const void *v;          /* (batch, seqlen_k, heads_k, head_dim)           */
+    void       *o;          /* (batch, seqlen_q, heads,   head_dim)           */
+    float      *lse;        /* (batch, heads, seqlen_q) fp32, or NULL         */
+
+    int32_t batch;
+    int32_t seqlen_q;
+    int32_t seqlen_k;
+    int32_t heads;
+    int32_t heads_k;        /* must equal heads (see flash_api.cpp:29)        */
+    int32_t head_dim;       /* 64 or 128                                      */
+
+    int64_t q_batch_stride, q_row_stride, q_head_stride;
+    int64_t k_batch_stride, k_row_stride, k_head_stride;
+    int64_t v_batch_stride, v_row_stride, v_head_stride;
+    int64_t o_batch_stride, o_row_stride, o_head_stride;
+    int64_t lse_batch_stride, lse_head_stride;   /* lse row stride is 1 */
+
+    float   softmax_scale;  /* the reference hard-wires 1/sqrt(head_dim)      */
+    int32_t is_causal;
+    int32_t is_bf16;        /* 0: fp16, 1: bf16                               */
+
+    /* Global position of query row 0 / key row 0 of this call.  The causal
+     * test is (key_offset + j) > (query_offset + i).  Both 0 for a plain call;
+     * sequence-sharded callers pass the chunk's position in the full sequence. */
+    int64_t q_pos_offset;
+    int64_t k_pos_offset;
+
+    /* Optional device int32 that receives FA_ERR_TIMEOUT if a bounded wait
+     * inside the kernel expires (the kernel then frees its tensor memory and
+     * returns instead of hanging).  NULL: the library's own flag is used. */
+    int32_t *error_flag;
+} FaParams;
+
+/* Validate params without launching anything (host only, no GPU needed). */
+FA_API int fa_sm100_check_params(const FaParams *p);
+
+/* Attention forward on `stream` (a cudaStream_t; 0 = legacy default stream).
+ * Asynchronous; returns FA_OK once the kernel is enqueued. */
+FA_API int fa_sm100_fwd(const FaParams *p, void *stream);
+
+/* Merge n partial results of the same query rows computed over disjoint key
+ * sets:  lse = log(sum_i exp(lse_i)),  O = sum_i exp(lse_i - lse) * O_i.
+ * o_parts: n pointers to fp32 (rows, heads, head_dim) contiguous partial O;
+ * lse_parts: n pointers to fp32 (heads, rows) partial LSE;
+ * o_out: (rows, heads, head_dim) fp16/bf16 with row stride o_row_stride and
+ * head stride o_head_stride (elements); lse_out: (heads, rows) fp32 or NULL. */
+FA_API int fa_sm100_lse_merge(const float *const *o_parts, const float *const *lse_parts,
+                       int32_t n_parts, int32_t rows, int32_t heads,
+                       int32_t head_dim, void *o_out, int64_t o_row_stride,
+                       int64_t o_head_stride, int32_t out_is_bf16,
+                       float *lse_out, void *stream);
+
+/* Host-readable copy of the library's device error flag for `device`
+ * (synchronises that device).  Returns FA_OK or the recorded error, and
+ * clears it. */
+FA_API int fa_sm100_take_device_error(int device);
+
+/* Human-readable text for a status code. */
+FA_API const char *fa_sm100_status_string(int status);
+
+/* Number of SMs the launcher sizes its persistent grid for (0 if unknown). */
+FA_API int fa_sm100_num_sms(int device);
+
+/* sizeof(FaParams) as compiled into the library, so an FFI binding can check
+ * its own struct mirror before the first call. */
+FA_API int fa_sm100_params_size(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* FA_SM100_H_ */

@@ -1,0 +1,191 @@
+"""Parity of the sm_100a kernel against the CPU oracle (fp32 math attention).
+
+Tolerances are the north star's: max |O - O_ref| <= 2e-3 (fp16), <= 1e-2
+(bf16); max |LSE - LSE_ref| <= 1e-3.  The grid extends the reference's own
+test (tests/test_flash_attn.py:17-23: batch {1,4} x seqlen {128,256,512} x
+heads 8 x head_dim {64,128}, fp16, non-causal) to causal and bf16, and adds
+sequence tails, unequal lengths, strided views, position offsets,
+determinism and direct C-ABI calls.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from oracle.attention_oracle import make_inputs, math_attention
+
+pytestmark = pytest.mark.gpu
+
+O_TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+LSE_TOL = 1e-3
+
+
+def _lse_err(lse, lse_ref):
+    a, b = lse.float().cpu(), lse_ref
+    both_inf = torch.isneginf(a) & torch.isneginf(b)
+    assert torch.equal(torch.isneginf(a), torch.isneginf(b)), "LSE -inf pattern differs"
+    d = (a - b).abs()
+    d[both_inf] = 0
+    return d.max().item() if d.numel() else 0.0
+
+
+def check(b, sq, h, d, dtype, causal, seed=0, sk=None, **oracle_kw):
+    from flash_attention import flash_attn_func
+
+    q, k, v = make_inputs(b, sq, h, d, dtype, seed=seed, seqlen_k=sk)
+    o, lse = flash_attn_func(q.cuda(), k.cuda(), v.cuda(), causal, return_lse=True)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = math_attention(q, k, v, causal, **oracle_kw)
+    err_o = (o.float().cpu() - o_ref).abs().max().item() if o.numel() else 0.0
+    err_l = _lse_err(lse, lse_ref)
+    assert o.shape == q.shape and o.dtype == q.dtype and o.stride() == q.stride()
+    assert err_o <= O_TOL[dtype], f"O max err {err_o}"
+    assert err_l <= LSE_TOL, f"LSE max err {err_l}"
+    return err_o, err_l
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("seqlen", [128, 256, 512])
+@pytest.mark.parametrize("batch", [1, 4])
+def test_reference_grid(batch, seqlen, head_dim, causal, dtype):
+    check(batch, seqlen, 8, head_dim, dtype, causal, seed=42)
+
+
+@pytest.mark.parametrize("sq,sk", [(1, 1), (7, 7), (65, 65), (127, 127), (129, 129), (200, 200),
+                                   (257, 257), (300, 300), (1000, 1000), (64, 300), (300, 64),
+                                   (1, 513), (513, 1)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_tails_and_unequal_lengths(sq, sk, causal):
+    check(2, sq, 3, 64, torch.bfloat16, causal, seed=sq * 1000 + sk, sk=sk)
+    check(1, sq, 2, 128, torch.float16, causal, seed=sq * 1000 + sk + 1, sk=sk)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_strided_packed_qkv(causal):
+    from flash_attention import flash_attn_func
+
+    b, s, h, d = 2, 333, 4, 128
+    g = torch.Generator().manual_seed(7)
+    qkv = torch.randn(b, s, 3, h, d, generator=g).to(torch.bfloat16)
+    q, k, v = qkv.unbind(2)
+    o, lse = flash_attn_func(q.cuda(), k.cuda(), v.cuda(), causal, return_lse=True)
+    qkv_d = qkv.cuda()
+    o2, lse2 = flash_attn_func(qkv_d[:, :, 0], qkv_d[:, :, 1], qkv_d[:, :, 2], causal, return_lse=True)
+    o_ref, lse_ref = math_attention(q, k, v, causal)
+    assert (o2.float().cpu() - o_ref).abs().max() <= O_TOL[torch.bfloat16]
+    assert _lse_err(lse2, lse_ref) <= LSE_TOL
+    assert torch.equal(o.cpu(), o2.cpu())
+
+
+def test_bhsd_transposed_views():
+    from flash_attention import flash_attn_func
+
+    b, s, h, d = 2, 200, 3, 64
+    g = torch.Generator().manual_seed(8)
+    x = [torch.randn(b, h, s, d, generator=g).half() for _ in range(3)]
+    q, k, v = (t.transpose(1, 2) for t in x)  # BSHD views of BHSD storage
+    o, lse = flash_attn_func(*(t.cuda().transpose(1, 2) for t in x), False, return_lse=True)
+    o_ref, lse_ref = math_attention(q, k, v, False)
+    assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.float16]
+    assert _lse_err(lse, lse_ref) <= LSE_TOL
+
+
+@pytest.mark.parametrize("q_off,k_off", [(0, 0), (512, 0), (1000, 512), (0, 100)])
+def test_position_offsets(q_off, k_off):
+    from flash_attention._C import forward_with_lse
+
+    q, k, v = make_inputs(1, 300, 2, 128, torch.bfloat16, seed=11, seqlen_k=700)
+    o, lse = forward_with_lse(q.cuda(), k.cuda(), v.cuda(), True, q_pos_offset=q_off, k_pos_offset=k_off)
+    o_ref, lse_ref = math_attention(q, k, v, True, q_pos_offset=q_off, k_pos_offset=k_off)
+    assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.bfloat16]
+    assert _lse_err(lse, lse_ref) <= LSE_TOL
+
+
+def test_empty_inputs():
+    from flash_attention import flash_attn_func
+
+    q = torch.zeros(0, 16, 2, 64, dtype=torch.float16, device="cuda")
+    assert flash_attn_func(q, q, q).shape == q.shape
+    q = torch.randn(1, 16, 2, 64, dtype=torch.float16, device="cuda")
+    kv = torch.zeros(1, 0, 2, 64, dtype=torch.float16, device="cuda")
+    o, lse = flash_attn_func(q, kv, kv, False, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.all(o == 0) and torch.all(torch.isneginf(lse))
+
+
+def test_deterministic_rerun():
+    from flash_attention import flash_attn_func
+
+    q, k, v = (t.cuda() for t in make_inputs(2, 777, 4, 128, torch.bfloat16, seed=12))
+    a = flash_attn_func(q, k, v, True, return_lse=True)
+    b = flash_attn_func(q, k, v, True, return_lse=True)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+def test_input_errors_on_gpu():
+    from flash_attention import flash_attn_func
+
+    q = torch.randn(1, 16, 2, 96, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="head_dim must be 64 or 128"):
+        flash_attn_func(q, q, q)
+    q = torch.randn(1, 16, 2, 64, dtype=torch.float32, device="cuda")
+    with pytest.raises(RuntimeError, match="q must be fp16 or bf16"):
+        flash_attn_func(q, q, q)
+    q = torch.randn(1, 16, 4, 64, dtype=torch.float16, device="cuda")
+    kv = torch.randn(1, 16, 3, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="heads must be divisible by heads_k"):
+        flash_attn_func(q, kv, kv)
+    x = torch.randn(1, 16, 2, 128, dtype=torch.float16, device="cuda")[..., ::2]
+    with pytest.raises(RuntimeError, match="contiguous in last dim"):
+        flash_attn_func(x, x, x)
+
+
+def test_c_abi_direct_call():
+    """Drive fa_sm100_fwd through ctypes with hand-filled FaParams (what a
+    non-Python caller does), on a non-default stream."""
+    from flash_attention import _C
+
+    b, s, h, d = 2, 384, 2, 64
+    q, k, v = make_inputs(b, s, h, d, torch.float16, seed=13)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o = torch.empty_like(qd)
+    lse = torch.empty(b, h, s, dtype=torch.float32, device="cuda")
+    p = _C.FaParams()
+    p.q, p.k, p.v, p.o, p.lse = qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), lse.data_ptr()
+    p.batch, p.seqlen_q, p.seqlen_k, p.heads, p.heads_k, p.head_dim = b, s, s, h, h, d
+    for name, t in (("q", qd), ("k", kd), ("v", vd), ("o", o)):
+        setattr(p, f"{name}_batch_stride", t.stride(0))
+        setattr(p, f"{name}_row_stride", t.stride(1))
+        setattr(p, f"{name}_head_stride", t.stride(2))
+    p.lse_batch_stride, p.lse_head_stride = lse.stride(0), lse.stride(1)
+    p.softmax_scale = 0.125
+    p.is_causal, p.is_bf16 = 1, 0
+    stream = torch.cuda.Stream()
+    rc = _C.lib.fa_sm100_fwd(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, _C.status_string(rc)
+    stream.synchronize()
+    assert _C.take_device_error(0) == 0
+    o_ref, lse_ref = math_attention(q, k, v, True)
+    assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.float16]
+    assert _lse_err(lse, lse_ref) <= LSE_TOL
+
+
+def test_lse_merge_recovers_full_attention():
+    from flash_attention._C import lse_merge
+
+    b, s, h, d = 1, 256, 3, 128
+    q, k, v = make_inputs(b, s, h, d, torch.bfloat16, seed=14, seqlen_k=600)
+    cuts = [0, 250, 600]
+    parts_o, parts_l = [], []
+    for c0, c1 in zip(cuts[:-1], cuts[1:]):
+        o_i, l_i = math_attention(q, k[:, c0:c1], v[:, c0:c1], True, k_pos_offset=c0, q_pos_offset=300)
+        parts_o.append(o_i[0].contiguous().cuda())
+        parts_l.append(l_i[0].contiguous().cuda())
+    out = torch.empty(s, h, d, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(h, s, dtype=torch.float32, device="cuda")
+    lse_merge(parts_o, parts_l, out, lse)
+    o_ref, lse_ref = math_attention(q, k, v, True, q_pos_offset=300)
+    assert (out.float().cpu() - o_ref[0]).abs().max() <= O_TOL[torch.bfloat16]
+    assert _lse_err(lse, lse_ref[0]) <= LSE_TOL
