@@ -314,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
     const int64_t key_lim = static_cast<int64_t>(row) + p.q_pos_offset - p.k_pos_offset;
 
     float m_run = -INFINITY;
-    float l_run = 0.f;
+    float l_run = 0.f;    // exact fp32 row sum (for the LSE)
+    float lr_run = 0.f;   // sum of the rounded P actually multiplied (bf16 only)
     bool ok = true;
     for (int j = 0; j < n_blocks; ++j) {
       // Every lane polls; the outcome is made warp-uniform because the
@@ -366,10 +367,12 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
           alpha = ex2_approx((m_run - m_new) * c);
           m_run = m_new;
           l_run *= alpha;
+          lr_run *= alpha;
         }
       }
       const float neg = (m_run == -INFINITY) ? 0.f : -m_run * c;
       float sum = 0.f;
+      float sum_r = 0.f;
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         uint32_t pk[16];
@@ -378,14 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
           const float p0 = ex2_approx(fmaf(s[h * 32 + 2 * i], c, neg));
           const float p1 = ex2_approx(fmaf(s[h * 32 + 2 * i + 1], c, neg));
           pk[i] = pack2<kBf16>(p0, p1);
+          sum += p0 + p1;
           if constexpr (kBf16) {
-            // Normalise by the sum of the bf16 values the MMA actually uses
-            // (the reference sums the unrounded fp32 values, kernel.cuh:233);
-            // with bf16's 8-bit mantissa the mismatch alone reaches ~3e-3 on
-            // rows that see few keys.
-            sum += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xffff0000u);
-          } else {
-            sum += p0 + p1;
+            // O is normalised by the sum of the bf16 values the MMA actually
+            // uses (the reference divides by the unrounded sum, kernel.cuh:233,
+            // which with bf16's 8-bit mantissa costs up to ~3e-3 on rows that
+            // see few keys); the LSE keeps the exact fp32 sum.
+            sum_r += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xffff0000u);
           }
         }
         tmem_st16(tS + h * 16, pk);
@@ -405,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
       }
       tmem_wait_st();
       l_run += sum;
+      lr_run += sum_r;
       tc_fence_before();
       mbar_arrive(smem_u32(&p_full[t]));
     }
@@ -416,7 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
                                                  static_cast<uint32_t>(n_blocks - 1) & 1u, vabort, tmo));
       tc_fence_after();
     }
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    const float l_norm = kBf16 ? lr_run : l_run;
+    const float inv = l_norm > 0.f ? 1.f / l_norm : 0.f;
     using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
     T* orow = reinterpret_cast<T*>(p.o) + static_cast<int64_t>(batch) * p.o_batch_stride +
               static_cast<int64_t>(row) * p.o_row_stride + static_cast<int64_t>(head) * p.o_head_stride;
