@@ -55,7 +55,12 @@ struct FwdKernelParams {
 
 constexpr int kBlockM = 128;  // query rows per tile (= TMEM lanes)
 constexpr int kBlockN = 128;  // keys per block
-constexpr int kThreads = 320;
+// Warps 0-3 / 4-7: softmax of query tile 0 / 1; warp 8: TMA producer;
+// warp 9: MMA issuer (and TMEM owner); warps 10-11 complete warpgroup 2.
+constexpr int kThreads = 384;
+constexpr uint32_t kRegsSoftmax = 200;
+constexpr uint32_t kRegsAux = 96;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsAux <= kThreads * 168, "register split exceeds launch budget");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -65,11 +70,73 @@ struct FwdTraits {
   static constexpr int kBoxBytes = kBlockM * 128;     // one 64-column (128-byte) TMA box
   static constexpr int kNumBoxes = D / 64;
   static constexpr int kStages = D == 128 ? 4 : 8;
+  // q_full[2], kv_full/empty[NS], s_full/p_full/pv_done[2], mma_drain
   static constexpr int kNumBarriers = 2 + 2 * kStages + 2 + 2 + 2 + 1;
   static constexpr int kSmemBytes =
       1024 /*alignment slack*/ + (2 + kStages) * kTileBytes + kNumBarriers * 8 + 16;
   static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + D;
+  // P (128 x 128 16-bit = 64 columns) gets its own columns when they fit
+  // (head_dim 64: 384 + 128 = 512); at head_dim 128 it is written over the
+  // first half of S.
+  static constexpr bool kPAliasesS = 2 * 128 + 2 * D + 2 * 64 > 512;
+  static constexpr uint32_t kColP0 = kPAliasesS ? kColS0 : 256 + 2 * D;
+  static constexpr uint32_t kColP1 = kPAliasesS ? kColS1 : 256 + 2 * D + 64;
 };
+
+// Pairs (out of every 16) whose exp2 runs on the FMA pipe (exp2_poly2)
+// instead of MUFU: at head_dim 128 the MUFU unit alone needs as many cycles
+// as the tensor core per block, so part of the work is moved.
+constexpr int kEmuPer16 = 5;
+__host__ __device__ constexpr bool emulated_pair(int i) { return (i * kEmuPer16) % 16 < kEmuPer16; }
+
+// P = exp2(s * c + neg) for one N-key slice of a row: packs P to 16-bit
+// pairs, stores them to TMEM at tP (N/2 columns per key half, 16x32bx2
+// layout), and returns the fp32 sum
+// and, for bf16, the sum of the rounded values.  kEmulate: use the
+// polynomial for the pairs picked by emulated_pair (only valid when no score
+// of the slice is -inf).
+template <bool kBf16, bool kEmulate, int N>
+__device__ __forceinline__ void exp_store_p(const float (&s)[N], float c, float neg, uint32_t tP, float& sum,
+                                            float& sum_r) {
+  const float2 c2 = make_float2(c, c);
+  const float2 n2 = make_float2(neg, neg);
+  float2 acc[4];
+  float accr[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    acc[k] = make_float2(0.f, 0.f);
+    accr[k] = 0.f;
+  }
+#pragma unroll
+  for (int h = 0; h < N / 32; ++h) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 x = __ffma2_rn(make_float2(s[h * 32 + 2 * i], s[h * 32 + 2 * i + 1]), c2, n2);
+      float2 e;
+      if (kEmulate && emulated_pair(i)) {
+        e = exp2_poly2(x);
+      } else {
+        e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+      }
+      pk[i] = pack2<kBf16>(e.x, e.y);
+      acc[i & 3] = __fadd2_rn(acc[i & 3], e);
+      if constexpr (kBf16) {
+        // O is normalised by the sum of the bf16 values the MMA actually
+        // multiplies (the reference divides by the unrounded sum,
+        // kernel.cuh:233, which with bf16's 8-bit mantissa costs up to ~3e-3
+        // on rows that see few keys); the LSE keeps the exact fp32 sum.
+        add_pair16_f32<true>(accr[i & 3], pk[i]);
+      }
+    }
+    // threads 0-15 write P columns [h*16, h*16+16) of their rows, threads
+    // 16-31 the same columns of the second key half (32 columns further).
+    tmem_st_16x32bx2_x16<N / 2>(tP + h * 16, pk);
+  }
+  const float2 a = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+  sum = a.x + a.y;
+  sum_r = kBf16 ? (accr[0] + accr[1]) + (accr[2] + accr[3]) : sum;
+}
 
 template <int D, bool kBf16, bool kCausal>
 __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_constant__ FwdKernelParams p) {
@@ -131,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&s_full[t]), 1);
-      mbar_init(smem_u32(&p_full[t]), kBlockM);
+      mbar_init(smem_u32(&p_full[t]), 2 * kBlockM);  // all 8 softmax warps
       mbar_init(smem_u32(&pv_done[t]), 1);
     }
     mbar_init(smem_u32(mma_drain), 1);
@@ -151,22 +218,53 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
   const uint32_t tmem = *tmem_holder;
   const uint64_t tmo = p.timeout_ns;
   const bool live = *vabort == 0;
+  // Register split (launch: 384 threads x 168): the producer / MMA warpgroup
+  // gives registers back so the two softmax warpgroups can hold a whole S row
+  // plus temporaries: 2 x 128 x 224 + 128 x 56 = 384 x 168.
+
+  // Each role ends here (no code after the role branches, so every branch
+  // keeps its own register budget).  In the producer / MMA warps lane 0
+  // arrives after the other lanes: reconverge first.
+  auto teardown = [&]() {
+    __syncwarp();
+    tc_fence_before();
+    asm volatile("barrier.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (warp == 9) {
+      __syncwarp();
+      tc_fence_after();
+      tmem_dealloc(tmem, kTmemCols);
+    }
+    if (threadIdx.x == 0 && *vabort == 1 && p.error_flag != nullptr) {
+      atomicExch(p.error_flag, -6 /* FA_ERR_TIMEOUT */);
+    }
+  };
   if (!live) n_blocks = 0;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && n_blocks > 0) {
-      prefetch_tmap(&p.tm_q);
-      prefetch_tmap(&p.tm_k);
-      prefetch_tmap(&p.tm_v);
+  if (warp >= 8) {
+    // Warpgroup 2: one register release for all four warps, then roles.
+    reg_dealloc<kRegsAux>();
+    // The producer and MMA warps run their loops with all 32 lanes
+    // (waits are warp-wide, warp-uniform); only lane 0 issues the TMA copies,
+    // the tcgen05.mma instructions and the commits.
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, vabort, tmo));
+    };
+    const bool leader = lane == 0;
+    if (warp == 8 && n_blocks > 0) {
+      // ---------------------------------------------------------- producer
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      for (int t = 0; t < 2; ++t) {
-        const uint32_t bar = smem_u32(&q_full[t]);
-        mbar_arrive_expect_tx(bar, Tr::kTileBytes);
-        for (int bx = 0; bx < Tr::kNumBoxes; ++bx) {
-          tma_load_4d(smem_u32(sQ + t * Tr::kTileBytes + bx * Tr::kBoxBytes), &p.tm_q, bar, bx * 64,
-                      head, m0 + t * kBlockM, batch, pol_q);
+      if (leader) {
+        prefetch_tmap(&p.tm_q);
+        prefetch_tmap(&p.tm_k);
+        prefetch_tmap(&p.tm_v);
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t bar = smem_u32(&q_full[t]);
+          mbar_arrive_expect_tx(bar, Tr::kTileBytes);
+          for (int bx = 0; bx < Tr::kNumBoxes; ++bx) {
+            tma_load_4d(smem_u32(sQ + t * Tr::kTileBytes + bx * Tr::kBoxBytes), &p.tm_q, bar, bx * 64, head,
+                        m0 + t * kBlockM, batch, pol_q);
+          }
         }
       }
       int it = 0;
@@ -175,16 +273,18 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
         for (int kv = 0; kv < 2; ++kv, ++it) {
           const int slot = it % NS;
           const uint32_t fill = static_cast<uint32_t>(it / NS);
-          if (!mbar_wait(smem_u32(&kv_empty[slot]), (fill & 1u) ^ 1u, vabort, tmo)) {
+          if (!wait_all(&kv_empty[slot], (fill & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          const uint32_t bar = smem_u32(&kv_full[slot]);
-          mbar_arrive_expect_tx(bar, Tr::kTileBytes);
-          const CUtensorMap* tm = kv == 0 ? &p.tm_k : &p.tm_v;
-          for (int bx = 0; bx < Tr::kNumBoxes; ++bx) {
-            tma_load_4d(smem_u32(sKV + slot * Tr::kTileBytes + bx * Tr::kBoxBytes), tm, bar, bx * 64,
-                        head, j * kBlockN, batch, pol_kv);
+          if (leader) {
+            const uint32_t bar = smem_u32(&kv_full[slot]);
+            mbar_arrive_expect_tx(bar, Tr::kTileBytes);
+            const CUtensorMap* tm = kv == 0 ? &p.tm_k : &p.tm_v;
+            for (int bx = 0; bx < Tr::kNumBoxes; ++bx) {
+              tma_load_4d(smem_u32(sKV + slot * Tr::kTileBytes + bx * Tr::kBoxBytes), tm, bar, bx * 64, head,
+                          j * kBlockN, batch, pol_kv);
+            }
           }
         }
       }
@@ -200,270 +300,297 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
           mbar_wait(smem_u32(&kv_full[s]), static_cast<uint32_t>(last / NS) & 1u, never, drain_ns);
         }
       }
-    }
-  } else if (warp == 9) {
-    // ----------------------------------------------------------------- MMA
-    if (lane == 0 && n_blocks > 0) {
+    } else if (warp == 9 && n_blocks > 0) {
+      // --------------------------------------------------------------- MMA
       constexpr uint32_t kIdescS = make_idesc_f16(kBlockM, kBlockN, kBf16, false);
       constexpr uint32_t kIdescO = make_idesc_f16(kBlockM, D, kBf16, true);
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t kv_addr = smem_u32(sKV);
       bool issued = false;
 
-      auto issue_s = [&](int t, uint32_t k_tile) {
+      // Descriptors are built once; per MMA only the start-address field
+      // (bits 0-13, 16-byte units) advances, so the issuing thread spends
+      // about one add per tcgen05.mma.  Addresses stay below 2^18 bytes, so
+      // the field never carries into the next one.
+      const uint64_t desc_q0 = make_sw128_desc(q_addr, 16, 1024);
+      const uint64_t desc_q1 = make_sw128_desc(q_addr + Tr::kTileBytes, 16, 1024);
+      const uint64_t desc_kv0 = make_sw128_desc(kv_addr, 16, 1024);
+      const uint64_t desc_v0 = make_sw128_desc(kv_addr, Tr::kBoxBytes, 1024);
+      constexpr uint64_t kSlotStep = Tr::kTileBytes >> 4;
+      auto issue_s = [&](int t, int slot) {
         // S_t = Q_t K^T : reduction over D in steps of 16 (32 bytes inside
         // a 128-byte swizzle row; a new 64-column box every 4 steps).
+        if (leader) {
+          const uint64_t a0 = t ? desc_q1 : desc_q0;
+          const uint64_t b0 = desc_kv0 + slot * kSlotStep;
+          const uint32_t d = tmem + (t ? Tr::kColS1 : Tr::kColS0);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * Tr::kBoxBytes + (kk & 3) * 32;
-          const uint64_t a = make_sw128_desc(q_addr + t * Tr::kTileBytes + off, 16, 1024);
-          const uint64_t b = make_sw128_desc(k_tile + off, 16, 1024);
-          umma_ss(tmem + (t ? Tr::kColS1 : Tr::kColS0), a, b, kIdescS, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t off = ((kk >> 2) * Tr::kBoxBytes + (kk & 3) * 32) >> 4;
+            umma_ss(d, a0 + off, b0 + off, kIdescS, kk > 0 ? 1u : 0u);
+          }
         }
+        __syncwarp();
       };
-      auto issue_pv = [&](int t, uint32_t v_tile, bool acc) {
+      auto issue_pv = [&](int t, int slot, bool acc) {
         // O_t += P_t V : reduction over the 128 keys in steps of 16.  P is
         // read from TMEM (16 keys = 8 columns of packed pairs); V is an
         // MN-major operand: 8-row groups 1024 B apart (SBO), 64-column boxes
-        // kBoxBytes apart (LBO).
+        // kBoxBytes apart (LBO); 16 keys = 2048 bytes.
+        if (leader) {
+          const uint64_t b0 = desc_v0 + slot * kSlotStep;
+          const uint32_t d = tmem + (t ? Tr::kColO1 : Tr::kColO0);
+          const uint32_t a = tmem + (t ? Tr::kColP1 : Tr::kColP0);
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          const uint64_t b = make_sw128_desc(v_tile + kk * 16 * 128, Tr::kBoxBytes, 1024);
-          umma_ts(tmem + (t ? Tr::kColO1 : Tr::kColO0), tmem + (t ? Tr::kColS1 : Tr::kColS0) + kk * 8, b, kIdescO,
-                  (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBlockN / 16; ++kk) {
+            umma_ts(d, a + kk * 8, b0 + kk * (2048 >> 4), kIdescO, (acc || kk > 0) ? 1u : 0u);
+          }
         }
+        __syncwarp();
+      };
+      auto commit = [&](uint64_t* bar) {
+        if (leader) umma_commit(smem_u32(bar));
+        __syncwarp();
       };
 
-      bool ok = mbar_wait(smem_u32(&q_full[0]), 0, vabort, tmo) &&
-                mbar_wait(smem_u32(&q_full[1]), 0, vabort, tmo);
+      bool ok = wait_all(&q_full[0], 0) && wait_all(&q_full[1], 0);
       int it = 0;
       if (ok) {
         const int slot = it % NS;
-        ok = mbar_wait(smem_u32(&kv_full[slot]), static_cast<uint32_t>(it / NS) & 1u, vabort, tmo);
+        ok = wait_all(&kv_full[slot], static_cast<uint32_t>(it / NS) & 1u);
         if (ok) {
           tc_fence_after();
-          const uint32_t k_tile = kv_addr + slot * Tr::kTileBytes;
-          issue_s(0, k_tile);
-          umma_commit(smem_u32(&s_full[0]));
-          issue_s(1, k_tile);
-          umma_commit(smem_u32(&s_full[1]));
-          umma_commit(smem_u32(&kv_empty[slot]));
+          issue_s(0, slot);
+          commit(&s_full[0]);
+          issue_s(1, slot);
+          commit(&s_full[1]);
+          commit(&kv_empty[slot]);
           issued = true;
           ++it;
         }
       }
+      // Per block j and tile t the tensor pipe runs O_t += P_t V_j and then,
+      // straight after it, S_t = Q_t K_{j+1}^T, so tile t's next scores are
+      // ready while the other tile's softmax runs.  When P_t is written over
+      // S_t (head_dim 128) this relies on the MMAs of one issuing thread
+      // executing in issue order: the P.V product reads its A operand before
+      // the following S MMA writes those columns.
       for (int j = 0; j < n_blocks && ok; ++j) {
         const uint32_t ph = static_cast<uint32_t>(j) & 1u;
+        const bool more = j + 1 < n_blocks;
         const int vslot = it % NS;
-        ok = mbar_wait(smem_u32(&kv_full[vslot]), static_cast<uint32_t>(it / NS) & 1u, vabort, tmo);
+        ok = wait_all(&kv_full[vslot], static_cast<uint32_t>(it / NS) & 1u);
         if (!ok) break;
-        const uint32_t v_tile = kv_addr + vslot * Tr::kTileBytes;
         ++it;
-        ok = mbar_wait(smem_u32(&p_full[0]), ph, vabort, tmo);
+        int kslot = 0;
+        ok = wait_all(&p_full[0], ph);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(0, v_tile, j > 0);
-        umma_commit(smem_u32(&pv_done[0]));
-        ok = mbar_wait(smem_u32(&p_full[1]), ph, vabort, tmo);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(1, v_tile, j > 0);
-        umma_commit(smem_u32(&pv_done[1]));
-        umma_commit(smem_u32(&kv_empty[vslot]));
-        if (j + 1 < n_blocks) {
-          const int kslot = it % NS;
-          ok = mbar_wait(smem_u32(&kv_full[kslot]), static_cast<uint32_t>(it / NS) & 1u, vabort, tmo);
+        issue_pv(0, vslot, j > 0);
+        commit(&pv_done[0]);
+        if (more) {
+          kslot = it % NS;
+          ok = wait_all(&kv_full[kslot], static_cast<uint32_t>(it / NS) & 1u);
           if (!ok) break;
-          const uint32_t k_tile = kv_addr + kslot * Tr::kTileBytes;
           ++it;
-          // P_t of block j sits in the S_t columns: S_t of block j+1 may only
-          // be written once the P.V product that reads it has completed.
-          ok = mbar_wait(smem_u32(&pv_done[0]), ph, vabort, tmo);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(0, k_tile);
-          umma_commit(smem_u32(&s_full[0]));
-          ok = mbar_wait(smem_u32(&pv_done[1]), ph, vabort, tmo);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(1, k_tile);
-          umma_commit(smem_u32(&s_full[1]));
-          umma_commit(smem_u32(&kv_empty[kslot]));
+          issue_s(0, kslot);
+          commit(&s_full[0]);
+        }
+        ok = wait_all(&p_full[1], ph);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(1, vslot, j > 0);
+        commit(&pv_done[1]);
+        commit(&kv_empty[vslot]);
+        if (more) {
+          issue_s(1, kslot);
+          commit(&s_full[1]);
+          commit(&kv_empty[kslot]);
         }
       }
       if (issued) {
-        // Make sure every MMA this thread issued has finished before TMEM is
+        // Make sure every MMA this warp issued has finished before TMEM is
         // released (matters only on the error path).
-        umma_commit(smem_u32(mma_drain));
+        commit(mma_drain);
         int zero = 0;
         volatile int* never = &zero;
         mbar_wait(smem_u32(mma_drain), 0, never, 200ull * 1000 * 1000);
       }
     }
+    teardown();
+    return;
   } else {
     // ------------------------------------------------------------- softmax
-    const int t = warp >> 2;       // query tile of this warpgroup
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int r = quarter * 32 + lane;
-    const int row = m0 + t * kBlockM + r;  // local query row
-    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + (t == 0 ? Tr::kColS0 : Tr::kColS1);
-    const uint32_t tO = tmem + lane_addr + (t == 0 ? Tr::kColO0 : Tr::kColO1);
+    // All 8 softmax warps work on one query tile at a time (tile 0, then
+    // tile 1, for every key block).  Warp w owns 16 of the 32 TMEM lanes of
+    // its quarter (w & 3): rows 32*(w&3) + 16*(w>>2) + [0,16).  With the
+    // 16x32bx2 access shape, thread t holds row (t & 15) and key half
+    // (t >> 4) of the block's 128 keys, so a row's two halves live in lanes
+    // t and t^16 of the same warp and combine with one shuffle.
+    reg_alloc<kRegsSoftmax>();
+    const int key_half = lane >> 4;
+    const int r = 32 * (warp & 3) + 16 * (warp >> 2) + (lane & 15);  // row within a tile
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * (warp & 3) + 16 * (warp >> 2)) << 16;
     const float c = p.scale_log2;
-    // Highest key index this row may see (causal), in local key numbering.
-    const int64_t key_lim = static_cast<int64_t>(row) + p.q_pos_offset - p.k_pos_offset;
+    constexpr int kHalfN = kBlockN / 2;
+    constexpr int kHalfD = D / 2;
 
-    float m_run = -INFINITY;
-    float l_run = 0.f;    // exact fp32 row sum (for the LSE)
-    float lr_run = 0.f;   // sum of the rounded P actually multiplied (bf16 only)
+    // Running state of the tile processed in this step (m, l, lr) and of
+    // the other tile (…o); swapped after every step, so the loop body exists
+    // once in the binary instead of once per tile.
+    float m_cur = -INFINITY, l_cur = 0.f, lr_cur = 0.f;  // lr: sum of rounded P (bf16)
+    float m_oth = -INFINITY, l_oth = 0.f, lr_oth = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_blocks; ++j) {
+#pragma unroll 1
+    for (int step = 0; step < 2 * n_blocks; ++step) {
+      const int t = step & 1;
+      const int j = step >> 1;
+      const uint32_t ph = static_cast<uint32_t>(j) & 1u;
       // Every lane polls; the outcome is made warp-uniform because the
       // tcgen05.ld / st that follow are warp-collective.
-      const bool got = __all_sync(0xffffffffu,
-                                  mbar_wait(smem_u32(&s_full[t]), static_cast<uint32_t>(j) & 1u, vabort, tmo));
-      if (!got) {
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[t]), ph, vabort, tmo))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[kBlockN];
+      const uint32_t col_s = t ? Tr::kColS1 : Tr::kColS0;
+      float s[kHalfN];
       {
-        uint32_t raw[32];
+        uint32_t raw[kHalfN];
+        tmem_ld_16x32bx2_x64_sync<kHalfN>(tmem + lane_addr + col_s, raw);
 #pragma unroll
-        for (int cc = 0; cc < kBlockN / 32; ++cc) {
-          tmem_ld32(tS + cc * 32, raw);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[cc * 32 + i] = __uint_as_float(raw[i]);
-        }
+        for (int i = 0; i < kHalfN; ++i) s[i] = __uint_as_float(raw[i]);
       }
-      // Mask keys past the end of the sequence and, if causal, keys after the row.
-      const int col0 = j * kBlockN;
+      // Mask keys past the end of the sequence and, if causal, keys after
+      // the row (key k visible to row i iff k + k_off <= i + q_off).
+      const int row = m0 + t * kBlockM + r;
+      const int col0 = j * kBlockN + key_half * kHalfN;
       int64_t valid = static_cast<int64_t>(p.seqlen_k) - col0;
       if constexpr (kCausal) {
-        const int64_t cl = key_lim - col0 + 1;
+        const int64_t cl = static_cast<int64_t>(row) + p.q_pos_offset - p.k_pos_offset - col0 + 1;
         valid = cl < valid ? cl : valid;
       }
-      if (valid < kBlockN) {
+      const bool masked = valid < kHalfN;
+      if (masked) {
 #pragma unroll
-        for (int i = 0; i < kBlockN; ++i) {
+        for (int i = 0; i < kHalfN; ++i) {
           if (i >= valid) s[i] = -INFINITY;
         }
       }
-      float mx = s[0];
+      // Row max: 8 independent 3-input max chains over this half, then the
+      // other half from lane t^16.
+      float mx8[8];
 #pragma unroll
-      for (int i = 1; i < kBlockN; ++i) mx = fmaxf(mx, s[i]);
-      const float m_new = fmaxf(m_run, mx);
-      bool warp_rescale = false;
-      float alpha = 1.f;
-      if (j == 0) {
-        m_run = m_new;
-      } else {
-        const bool need =
-            (m_new > m_run) && (m_run == -INFINITY || (m_new - m_run) * c > kRescaleThreshold);
-        warp_rescale = __any_sync(0xffffffffu, need);
-        if (need) {
-          alpha = ex2_approx((m_run - m_new) * c);
-          m_run = m_new;
-          l_run *= alpha;
-          lr_run *= alpha;
-        }
+      for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(s[k], s[k + 8]);
+#pragma unroll
+      for (int i = 16; i < kHalfN; i += 16) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], s[i + k], s[i + 8 + k]);
       }
-      const float neg = (m_run == -INFINITY) ? 0.f : -m_run * c;
-      float sum = 0.f;
-      float sum_r = 0.f;
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(s[h * 32 + 2 * i], c, neg));
-          const float p1 = ex2_approx(fmaf(s[h * 32 + 2 * i + 1], c, neg));
-          pk[i] = pack2<kBf16>(p0, p1);
-          sum += p0 + p1;
-          if constexpr (kBf16) {
-            // O is normalised by the sum of the bf16 values the MMA actually
-            // uses (the reference divides by the unrounded sum, kernel.cuh:233,
-            // which with bf16's 8-bit mantissa costs up to ~3e-3 on rows that
-            // see few keys); the LSE keeps the exact fp32 sum.
-            sum_r += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xffff0000u);
-          }
-        }
-        tmem_st16(tS + h * 16, pk);
+      const float pm = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+      const float m_new = fmax3(pm, __shfl_xor_sync(0xffffffffu, pm, 16), m_cur);
+      // Both halves of a row see identical values, so they decide alike.
+      // The running max is only raised when it grew by more than 2^8
+      // (kRescaleThreshold in log2 units); P then stays <= 2^8 and the final
+      // division uses the same stale max, so the result is exact.
+      const bool need = (m_new > m_cur) && (m_cur == -INFINITY || (m_new - m_cur) * c > kRescaleThreshold);
+      const bool warp_rescale = (j > 0) && __any_sync(0xffffffffu, need);
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_approx((m_cur - m_new) * c);  // 0 when m_cur = -inf
+        m_cur = m_new;
+        l_cur *= alpha;
+        lr_cur *= alpha;
+      }
+      const float neg = (m_cur == -INFINITY) ? 0.f : -m_cur * c;
+      // P over the first 64 S columns (head_dim 128): every S value of this
+      // warp's rows was loaded (and waited for) above, by this warp.
+      const uint32_t tP = tmem + lane_addr + (t ? Tr::kColP1 : Tr::kColP0);
+      float sum, sum_r;
+      if (__any_sync(0xffffffffu, masked)) {
+        exp_store_p<kBf16, false, kHalfN>(s, c, neg, tP, sum, sum_r);
+      } else {
+        exp_store_p<kBf16, true, kHalfN>(s, c, neg, tP, sum, sum_r);
       }
       if (warp_rescale) {
-        // O_t of block j-1 is complete (S_t of block j was committed after its
-        // P.V product) and the next P.V waits for p_full: rescale it in place.
+        // O_t of block j-1 is complete (S_t of block j was committed after
+        // its P.V product) and the next P.V waits for p_full: rescale in
+        // place, each thread its key half's share of the O columns.
+        const uint32_t tO = tmem + lane_addr + (t ? Tr::kColO1 : Tr::kColO0);
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
+        for (int cc = 0; cc < kHalfD / 32; ++cc) {
           uint32_t o[32];
-          tmem_ld32(tO + cc * 32, o);
-          tmem_wait_ld();
+          tmem_ld_16x32bx2_x32_sync<kHalfD>(tO + cc * 32, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + cc * 32, o);
+          tmem_st_16x32bx2_x32<kHalfD>(tO + cc * 32, o);
         }
       }
       tmem_wait_st();
-      l_run += sum;
-      lr_run += sum_r;
+      l_cur += sum;
+      lr_cur += sum_r;
       tc_fence_before();
       mbar_arrive(smem_u32(&p_full[t]));
+      // next step works on the other tile
+      float tmp = m_cur; m_cur = m_oth; m_oth = tmp;
+      tmp = l_cur; l_cur = l_oth; l_oth = tmp;
+      tmp = lr_cur; lr_cur = lr_oth; lr_oth = tmp;
     }
+    // After an even number of steps "cur" is tile 0 again.
+    const float m_run[2] = {m_cur, m_oth};
+    const float l_run[2] = {l_cur, l_oth};
+    const float lr_run[2] = {lr_cur, lr_oth};
 
-    // ---- epilogue: O /= l, store O (and LSE).
-    bool have_o = ok && n_blocks > 0;
-    if (have_o) {
-      have_o = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]),
-                                                 static_cast<uint32_t>(n_blocks - 1) & 1u, vabort, tmo));
-      tc_fence_after();
-    }
-    const float l_norm = kBf16 ? lr_run : l_run;
-    const float inv = l_norm > 0.f ? 1.f / l_norm : 0.f;
+    // ---- epilogue: combine the halves' sums, O /= l, store O (and LSE).
     using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
-    T* orow = reinterpret_cast<T*>(p.o) + static_cast<int64_t>(batch) * p.o_batch_stride +
-              static_cast<int64_t>(row) * p.o_row_stride + static_cast<int64_t>(head) * p.o_head_stride;
-    const bool row_ok = live && row < p.seqlen_q;
 #pragma unroll
-    for (int cc = 0; cc < D / 32; ++cc) {
-      uint32_t o[32];
+    for (int t = 0; t < 2; ++t) {
+      const float l_tot = l_run[t] + __shfl_xor_sync(0xffffffffu, l_run[t], 16);
+      const float lr_tot = lr_run[t] + __shfl_xor_sync(0xffffffffu, lr_run[t], 16);
+      bool have_o = ok && n_blocks > 0;
       if (have_o) {
-        tmem_ld32(tO + cc * 32, o);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
+        have_o = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), static_cast<uint32_t>(n_blocks - 1) & 1u,
+                                                   vabort, tmo));
+        tc_fence_after();
       }
-      if (row_ok) {
-        uint32_t packed[16];
+      const float l_norm = kBf16 ? lr_tot : l_tot;
+      const float inv = l_norm > 0.f ? 1.f / l_norm : 0.f;
+      const int row = m0 + t * kBlockM + r;
+      const bool row_ok = live && row < p.seqlen_q;
+      T* orow = reinterpret_cast<T*>(p.o) + static_cast<int64_t>(batch) * p.o_batch_stride +
+                static_cast<int64_t>(row) * p.o_row_stride + static_cast<int64_t>(head) * p.o_head_stride +
+                key_half * kHalfD;
+      const uint32_t tO = tmem + lane_addr + (t ? Tr::kColO1 : Tr::kColO0);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          packed[i] = pack2<kBf16>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+      for (int cc = 0; cc < kHalfD / 32; ++cc) {
+        uint32_t o[32];
+        if (have_o) {
+          tmem_ld_16x32bx2_x32_sync<kHalfD>(tO + cc * 32, o);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
+        if (row_ok) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            packed[i] = pack2<kBf16>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          }
+        }
+      }
+      if (row_ok && key_half == 0 && p.lse != nullptr) {
+        const float lse = l_tot > 0.f ? fmaf(m_run[t], p.scale, logf(l_tot)) : -INFINITY;
+        p.lse[static_cast<int64_t>(batch) * p.lse_batch_stride + static_cast<int64_t>(head) * p.lse_head_stride +
+              row] = lse;
       }
     }
-    if (row_ok && p.lse != nullptr) {
-      const float lse = l_run > 0.f ? fmaf(m_run, p.scale, logf(l_run)) : -INFINITY;
-      p.lse[static_cast<int64_t>(batch) * p.lse_batch_stride + static_cast<int64_t>(head) * p.lse_head_stride +
-            row] = lse;
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
-  }
-  if (threadIdx.x == 0 && *vabort == 1 && p.error_flag != nullptr) {
-    atomicExch(p.error_flag, -6 /* FA_ERR_TIMEOUT */);
+    teardown();
+    return;
   }
 }
 
