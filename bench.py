@@ -51,6 +51,9 @@ CONFIGS = {
     "C2": dict(batch=8, seqlen=2048, heads=16, head_dim=128, dtype="bfloat16", causal=True),
     "C3": dict(batch=16, seqlen=4096, heads=32, head_dim=64, dtype="float16", causal=False),
     "C4": dict(batch=32, seqlen=4096, heads=64, head_dim=128, dtype="bfloat16", causal=False),
+    # Long-context causal attention; sharded by zigzag context parallelism
+    # (NCCL K/V all-gather) under torchrun, strong scaling.
+    "C5": dict(batch=1, seqlen=131072, heads=32, head_dim=128, dtype="bfloat16", causal=True),
     # Profiling case for ncu: C4's per-unit shape with 64 (batch, head) units;
     # q/k/v/o = 256 MiB (> L2) so DRAM counters stay meaningful.
     "C4s": dict(batch=4, seqlen=4096, heads=16, head_dim=128, dtype="bfloat16", causal=False),
@@ -316,6 +319,70 @@ def build_fn(impl, cfg, causal):
     return fn, "reference SM80 kernel (its own csrc, compiled for sm_100a) via _C.forward, O only"
 
 
+def run_context_parallel(a, dist_):
+    """C5: every rank builds the same seeded full q/k/v, keeps its zigzag
+    shard and runs the context-parallel forward (all-gather of K/V + two
+    kernel calls); the whole job is one causal attention over the sequence."""
+    from flash_attention import flash_attn_func
+    from flash_attention.distributed import context_parallel_attention, zigzag_shard
+
+    cfg = CONFIGS["C5"]
+    b, s, h, d = cfg["batch"], cfg["seqlen"], cfg["heads"], cfg["head_dim"]
+    q, k, v = make_shard(cfg, 0, dist_.dev)  # identical on every rank
+    if dist_.world > 1:
+        q, k, v = (zigzag_shard(t, dist_.world, dist_.rank) for t in (q, k, v))
+
+        def fn(q_, k_, v_):
+            return context_parallel_attention(q_, k_, v_, True)
+    else:
+
+        def fn(q_, k_, v_):
+            return flash_attn_func(q_, k_, v_, True, return_lse=True)
+
+    fl = flops(b, s, h, d, True)  # whole job
+    peak, _, peak_src = load_peaks()
+    clocks = ClockSampler(dist_.local) if not a.no_clocks else None
+    ms, launch_ms = device_timed(fn, (q, k, v), a.steps, a.warmup, dist_, clocks)
+    value = fl / (ms * 1e-3) / 1e12
+    if dist_.rank == 0:
+        line = {
+            "metric": "attn fwd TFLOPS (whole job) & fraction of measured B200 dense bf16 peak",
+            "value": round(value, 2),
+            "unit": "TFLOPS",
+            "n_gpus": a.gpus,
+            "steps": a.steps,
+            "warmup": a.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: i.i.d. N(0,1) q/k/v from a seeded generator (no dataset involved)",
+            "config": {
+                "workload": f"C5: causal attention b={b} s={s} h={h} d={d} bf16, O + LSE, one sequence over "
+                f"{a.gpus} GPU(s)",
+                "seq_len": s,
+                "parallelism": "zigzag context parallelism: 2N chunks, NCCL all-gather of K and V, "
+                "kernel on global positions" if a.gpus > 1 else "single GPU",
+                "l2": "inputs larger than L2 (q/k/v = 1 GiB each)",
+                "flops_per_step_total": fl,
+            },
+            "impl": a.impl,
+            "roofline": {
+                "bound": "tensor",
+                "achieved_per_gpu": round(value / a.gpus, 2),
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": round(value / a.gpus / peak, 4),
+                "peak_source": f"{peak_src} dense bf16 GEMM (burst)",
+            },
+            "gpu_launches": a.steps * (2 if a.gpus > 1 else 1),
+            "clocks": clocks.summary() if clocks is not None else None,
+        }
+        print(json.dumps(line), flush=True)
+    dist_.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -331,6 +398,15 @@ def main():
     a.warmup = max(a.warmup, 3)
 
     dist_ = Dist(a.gpus)
+    if a.config == "C5":
+        if a.impl == "reference":
+            if dist_.rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no context-parallel "
+                                  "path (single-GPU only); compare C5 at N=1 through --config C5 on one GPU"}))
+            dist_.close()
+            return
+        run_context_parallel(a, dist_)
+        return
     cfg = dict(CONFIGS[a.config])
     b, s, h, d = cfg["batch"], cfg["seqlen"], cfg["heads"], cfg["head_dim"]
     ref_available = True

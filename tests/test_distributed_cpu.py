@@ -1,0 +1,94 @@
+"""Host logic of the multi-GPU paths on CPU: gloo ranks (world size 2 and 4),
+the oracle standing in for the per-chunk kernel call."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from flash_attention.distributed import (
+    context_parallel_attention,
+    gather_zigzag,
+    shard_units,
+    zigzag_chunks,
+    zigzag_shard,
+    zigzag_unshard,
+)
+from oracle.attention_oracle import make_inputs, math_attention
+
+
+def test_shard_units_cover_everything_once():
+    for batch, heads, world in [(32, 64, 8), (3, 5, 4), (1, 1, 2), (7, 3, 5)]:
+        seen = []
+        for r in range(world):
+            a, b = shard_units(batch, heads, world, r)
+            seen.extend(range(a, b))
+        assert seen == list(range(batch * heads))
+
+
+def test_zigzag_chunks_balance_causal_work():
+    s, world = 1024, 4
+    c = s // (2 * world)
+    work = []
+    for r in range(world):
+        (a0, a1), (b0, b1) = zigzag_chunks(s, world, r)
+        assert a1 - a0 == c and b1 - b0 == c
+        # causal work of a chunk ~ sum of visible keys of its rows
+        work.append(sum(range(a0 + 1, a1 + 1)) + sum(range(b0 + 1, b1 + 1)))
+    assert max(work) == min(work)
+    with pytest.raises(ValueError):
+        zigzag_chunks(1000, 3, 0)
+
+
+def test_zigzag_shard_roundtrip():
+    x = torch.arange(2 * 48 * 3 * 2, dtype=torch.float32).view(2, 48, 3, 2)
+    parts = [zigzag_shard(x, 3, r) for r in range(3)]
+    assert torch.equal(zigzag_unshard(parts), x)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _oracle_attn(q, k, v, causal, q_pos_offset, out, lse_out):
+    o, lse = math_attention(q, k, v, causal, q_pos_offset=q_pos_offset)
+    out.copy_(o.to(out.dtype))
+    lse_out.copy_(lse)
+
+
+def _worker(rank, world, port, seqlen, causal, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        q, k, v = make_inputs(1, seqlen, 2, 64, torch.float32, seed=21)
+        ql, kl, vl = (zigzag_shard(t, world, rank) for t in (q, k, v))
+        # the gathered keys come back in sequence order
+        assert torch.equal(gather_zigzag(kl), k)
+        o, lse = context_parallel_attention(ql, kl, vl, causal, attn_fn=_oracle_attn)
+        outs = [torch.empty_like(o) for _ in range(world)]
+        lses = [torch.empty_like(lse) for _ in range(world)]
+        dist.all_gather(outs, o)
+        dist.all_gather(lses, lse)
+        if rank == 0:
+            o_full = zigzag_unshard(outs, dim=1)
+            lse_full = zigzag_unshard(lses, dim=2)
+            o_ref, lse_ref = math_attention(q, k, v, causal)
+            ret["o_err"] = (o_full - o_ref).abs().max().item()
+            ret["lse_err"] = (lse_full - lse_ref).abs().max().item()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,causal", [(2, True), (2, False), (4, True)])
+def test_context_parallel_matches_full_attention(world, causal):
+    seqlen = 64 * world
+    ret = mp.Manager().dict()
+    mp.start_processes(_worker, args=(world, _free_port(), seqlen, causal, ret), nprocs=world,
+                       start_method="spawn", join=True)
+    assert ret["o_err"] < 1e-5 and ret["lse_err"] < 1e-5, dict(ret)

@@ -1,0 +1,89 @@
+"""Context-parallel attention on GPUs against the fp32 oracle.
+
+test_cp_emulated_ranks runs every rank's share on one GPU (no collective) and
+checks the assembled output; test_cp_nccl runs real NCCL ranks when the box
+has at least two GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+
+from flash_attention.distributed import zigzag_chunks, zigzag_shard, zigzag_unshard
+from oracle.attention_oracle import make_inputs, math_attention
+
+pytestmark = pytest.mark.gpu
+
+O_TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+
+
+@pytest.mark.parametrize("world,dtype", [(2, torch.bfloat16), (4, torch.float16), (8, torch.bfloat16)])
+def test_cp_emulated_ranks(world, dtype):
+    from flash_attention._C import forward_with_lse
+
+    s = 4096
+    q, k, v = make_inputs(1, s, 2, 128, dtype, seed=31)
+    kd, vd = k.cuda(), v.cuda()
+    outs, lses = [], []
+    for r in range(world):
+        ql = zigzag_shard(q, world, r).cuda()
+        c = ql.size(1) // 2
+        o = torch.empty_like(ql)
+        lse = torch.empty(1, 2, 2 * c, dtype=torch.float32, device="cuda")
+        for i, ((g0, _g1)) in enumerate(zigzag_chunks(s, world, r)):
+            forward_with_lse(ql[:, i * c:(i + 1) * c], kd, vd, True, q_pos_offset=g0,
+                             out=o[:, i * c:(i + 1) * c], lse_out=lse[:, :, i * c:(i + 1) * c])
+        outs.append(o.cpu())
+        lses.append(lse.cpu())
+    o_full = zigzag_unshard(outs, dim=1)
+    lse_full = zigzag_unshard(lses, dim=2)
+    o_ref, lse_ref = math_attention(q, k, v, True)
+    assert (o_full.float() - o_ref).abs().max() <= O_TOL[dtype]
+    assert (lse_full - lse_ref).abs().max() <= 1e-3
+
+
+def _free_port():
+    with socket.socket() as sck:
+        sck.bind(("127.0.0.1", 0))
+        return sck.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, ret):
+    import datetime
+
+    import torch.distributed as dist
+
+    from flash_attention.distributed import context_parallel_attention
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        s = 2048
+        q, k, v = make_inputs(1, s, 2, 128, torch.bfloat16, seed=41)
+        ql, kl, vl = (zigzag_shard(t, world, rank).cuda() for t in (q, k, v))
+        o, lse = context_parallel_attention(ql, kl, vl, True)
+        outs = [torch.empty_like(o) for _ in range(world)]
+        lses = [torch.empty_like(lse) for _ in range(world)]
+        dist.all_gather(outs, o)
+        dist.all_gather(lses, lse)
+        torch.cuda.synchronize()
+        if rank == 0:
+            o_full = zigzag_unshard([t.cpu() for t in outs], dim=1)
+            lse_full = zigzag_unshard([t.cpu() for t in lses], dim=2)
+            o_ref, lse_ref = math_attention(q, k, v, True)
+            ret["o_err"] = (o_full.float() - o_ref).abs().max().item()
+            ret["lse_err"] = (lse_full - lse_ref).abs().max().item()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_cp_nccl():
+    import torch.multiprocessing as mp
+
+    ret = mp.Manager().dict()
+    mp.start_processes(_nccl_worker, args=(2, _free_port(), ret), nprocs=2, start_method="spawn", join=True)
+    assert ret["o_err"] <= O_TOL[torch.bfloat16] and ret["lse_err"] <= 1e-3, dict(ret)
