@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -98,8 +99,8 @@ int encode_operand(CUtensorMap* m, const void* base, bool bf16, int head_dim, in
 }
 
 // Bound on any single device-side wait.  FA_SM100_TIMEOUT_MS overrides the
-// 2 s default (read once per process).
-uint64_t timeout_ns() {
+// 2 s default (read once per process); fa_sm100_set_timeout_ns overrides both.
+uint64_t default_timeout_ns() {
   static const uint64_t ns = [] {
     const char* e = std::getenv("FA_SM100_TIMEOUT_MS");
     const long ms = e != nullptr ? std::strtol(e, nullptr, 10) : 0;
@@ -107,14 +108,19 @@ uint64_t timeout_ns() {
   }();
   return ns;
 }
+std::atomic<uint64_t> g_timeout_override{0};
+uint64_t timeout_ns() {
+  const uint64_t o = g_timeout_override.load(std::memory_order_relaxed);
+  return o != 0 ? o : default_timeout_ns();
+}
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 bool stride_ok(int64_t s) { return s >= 0 && (s % 8) == 0; }  // 16 bytes of 16-bit elements
 
-template <int D, bool BF16, bool CAUSAL>
+template <int D, bool BF16, bool CAUSAL, bool DIAG>
 int launch(const fa::FwdKernelParams& kp, cudaStream_t stream) {
   using Tr = fa::FwdTraits<D>;
-  auto kernel = fa::fa_fwd_sm100_kernel<D, BF16, CAUSAL>;
+  auto kernel = fa::fa_fwd_sm100_kernel<D, BF16, CAUSAL, DIAG>;
   cudaError_t e =
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return FA_ERR_CUDA;
@@ -125,9 +131,16 @@ int launch(const fa::FwdKernelParams& kp, cudaStream_t stream) {
   return e == cudaSuccess ? FA_OK : FA_ERR_CUDA;
 }
 
+// Wait bounds below 1 ms select the diagnostic instantiation whose waits
+// poll, so the bound can expire (see mbar_wait); production bounds never do.
+constexpr uint64_t kDiagBoundNs = 1000000ull;
+
 template <int D, bool BF16>
 int launch_causal(const fa::FwdKernelParams& kp, bool causal, cudaStream_t s) {
-  return causal ? launch<D, BF16, true>(kp, s) : launch<D, BF16, false>(kp, s);
+  if (kp.timeout_ns < kDiagBoundNs) {
+    return causal ? launch<D, BF16, true, true>(kp, s) : launch<D, BF16, false, true>(kp, s);
+  }
+  return causal ? launch<D, BF16, true, false>(kp, s) : launch<D, BF16, false, false>(kp, s);
 }
 
 }  // namespace
@@ -140,7 +153,7 @@ int fa_sm100_check_params(const FaParams* p) {
     return FA_ERR_INVALID_ARG;
   }
   if (p->head_dim != 64 && p->head_dim != 128) return FA_ERR_UNSUPPORTED;
-  if (p->heads_k != p->heads) return FA_ERR_UNSUPPORTED;
+  if (p->heads % p->heads_k != 0) return FA_ERR_INVALID_ARG;  // GQA / MQA groups
   if (!std::isfinite(p->softmax_scale)) return FA_ERR_INVALID_ARG;
   if (p->batch == 0 || p->seqlen_q == 0) return FA_OK;  // nothing to compute
   if (p->q == nullptr || p->o == nullptr) return FA_ERR_INVALID_ARG;
@@ -200,6 +213,7 @@ int fa_sm100_fwd(const FaParams* p, void* stream_ptr) {
   kp.seqlen_k = p->seqlen_k;
   kp.heads = p->heads;
   kp.batch = p->batch;
+  kp.heads_per_kv = p->heads / p->heads_k;
   kp.num_m_blocks = (p->seqlen_q + 2 * fa::kBlockM - 1) / (2 * fa::kBlockM);
   kp.scale = p->softmax_scale;
   kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
@@ -257,7 +271,7 @@ const char* fa_sm100_status_string(int status) {
   switch (status) {
     case FA_OK: return "ok";
     case FA_ERR_INVALID_ARG: return "invalid argument";
-    case FA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim must be 64 or 128, heads_k == heads, strides TMA-encodable)";
+    case FA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim must be 64 or 128, strides TMA-encodable)";
     case FA_ERR_ALIGNMENT: return "pointers must be 16-byte aligned and strides multiples of 8 elements";
     case FA_ERR_CUDA: return "CUDA error";
     case FA_ERR_NO_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
@@ -267,6 +281,11 @@ const char* fa_sm100_status_string(int status) {
 }
 
 int fa_sm100_params_size(void) { return static_cast<int>(sizeof(FaParams)); }
+
+uint64_t fa_sm100_set_timeout_ns(uint64_t ns) {
+  const uint64_t prev = g_timeout_override.exchange(ns, std::memory_order_relaxed);
+  return prev != 0 ? prev : default_timeout_ns();
+}
 
 int fa_sm100_num_sms(int device) {
   int n = 0;

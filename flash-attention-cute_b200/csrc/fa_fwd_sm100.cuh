@@ -48,6 +48,7 @@ struct FwdKernelParams {
   int64_t q_pos_offset, k_pos_offset;
   uint64_t timeout_ns;
   int seqlen_q, seqlen_k, heads, batch;
+  int heads_per_kv;  // query heads per K/V head (GQA / MQA group size)
   int num_m_blocks;  // ceil(seqlen_q / 256)
   float scale;       // softmax scale
   float scale_log2;  // softmax scale * log2(e)
@@ -138,7 +139,9 @@ __device__ __forceinline__ void exp_store_p(const float (&s)[N], float c, float 
   sum_r = kBf16 ? (accr[0] + accr[1]) + (accr[2] + accr[3]) : sum;
 }
 
-template <int D, bool kBf16, bool kCausal>
+// kDiag: the instantiation launched when the wait bound is below 1 ms (a
+// caller exercising the failure path); its waits poll so the bound expires.
+template <int D, bool kBf16, bool kCausal, bool kDiag>
 __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_constant__ FwdKernelParams p) {
   using Tr = FwdTraits<D>;
   constexpr int NS = Tr::kStages;
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
   }
   const int head = bh % p.heads;
   const int batch = bh / p.heads;
+  const int kv_head = head / p.heads_per_kv;  // K/V shared by a group of query heads
   const int m0 = m_block * 2 * kBlockM;
 
   int n_blocks = (p.seqlen_k + kBlockN - 1) / kBlockN;
@@ -247,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
     // (waits are warp-wide, warp-uniform); only lane 0 issues the TMA copies,
     // the tcgen05.mma instructions and the commits.
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, vabort, tmo));
+      return __all_sync(0xffffffffu, mbar_wait<kDiag>(smem_u32(bar), parity, vabort, tmo));
     };
     const bool leader = lane == 0;
     if (warp == 8 && n_blocks > 0) {
@@ -282,8 +286,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
             mbar_arrive_expect_tx(bar, Tr::kTileBytes);
             const CUtensorMap* tm = kv == 0 ? &p.tm_k : &p.tm_v;
             for (int bx = 0; bx < Tr::kNumBoxes; ++bx) {
-              tma_load_4d(smem_u32(sKV + slot * Tr::kTileBytes + bx * Tr::kBoxBytes), tm, bar, bx * 64, head,
-                          j * kBlockN, batch, pol_kv);
+              tma_load_4d(smem_u32(sKV + slot * Tr::kTileBytes + bx * Tr::kBoxBytes), tm, bar, bx * 64,
+                          kv_head, j * kBlockN, batch, pol_kv);
             }
           }
         }
@@ -448,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
       const uint32_t ph = static_cast<uint32_t>(j) & 1u;
       // Every lane polls; the outcome is made warp-uniform because the
       // tcgen05.ld / st that follow are warp-collective.
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[t]), ph, vabort, tmo))) {
+      if (!__all_sync(0xffffffffu, mbar_wait<kDiag>(smem_u32(&s_full[t]), ph, vabort, tmo))) {
         ok = false;
         break;
       }
@@ -549,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
       const float lr_tot = lr_run[t] + __shfl_xor_sync(0xffffffffu, lr_run[t], 16);
       bool have_o = ok && n_blocks > 0;
       if (have_o) {
-        have_o = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), static_cast<uint32_t>(n_blocks - 1) & 1u,
+        have_o = __all_sync(0xffffffffu, mbar_wait<kDiag>(smem_u32(&pv_done[t]), static_cast<uint32_t>(n_blocks - 1) & 1u,
                                                    vabort, tmo));
         tc_fence_after();
       }

@@ -48,22 +48,53 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the phase with parity `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with parity `parity` of barrier `bar` to complete.
 // Bounded: gives up after `timeout_ns` (or as soon as *abort is set by a
 // sibling warp that gave up), records the failure and returns false, so a
 // logic error in the pipeline ends the kernel instead of hanging the GPU.
+//
+// kPollOnly (diagnostic kernels, sub-millisecond bounds): poll with the
+// non-blocking test_wait and read the clock on every retry.  The default
+// form starts with try_wait, which may sleep until the phase completes --
+// the fastest wake-up, but it can outlast a bound of a few microseconds.
+template <bool kPollOnly = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           volatile int* abort_flag, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  uint32_t spins = 0;
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
+  if constexpr (kPollOnly) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_test_wait(bar, parity)) {
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > timeout_ns) {
         *abort_flag = 1;
         return false;
+      }
+    }
+    return true;
+  } else {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spins = 0;
+    while (true) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if ((++spins & 63u) == 0) {
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > timeout_ns) {
+          *abort_flag = 1;
+          return false;
+        }
       }
     }
   }

@@ -95,6 +95,8 @@ def _load() -> ctypes.CDLL:
     lib.fa_sm100_num_sms.restype = ctypes.c_int
     lib.fa_sm100_params_size.argtypes = []
     lib.fa_sm100_params_size.restype = ctypes.c_int
+    lib.fa_sm100_set_timeout_ns.argtypes = [ctypes.c_uint64]
+    lib.fa_sm100_set_timeout_ns.restype = ctypes.c_uint64
     if lib.fa_sm100_params_size() != ctypes.sizeof(FaParams):
         raise ImportError(
             f"FaParams layout mismatch: library {lib.fa_sm100_params_size()} bytes, "
@@ -140,10 +142,8 @@ def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
         raise RuntimeError("q, k and v must have the same dtype")
     if k.device != q.device or v.device != q.device:
         raise RuntimeError("q, k and v must be on the same device")
-    if k.size(2) != q.size(2):
-        raise RuntimeError("heads_k must equal heads (GQA/MQA is not supported by this kernel)")
     if k.shape != v.shape or k.size(0) != q.size(0) or k.size(3) != head_dim:
-        raise RuntimeError("k and v must be (batch, seqlen_k, heads, head_dim) matching q")
+        raise RuntimeError("k and v must be (batch, seqlen_k, heads_k, head_dim) matching q")
 
 
 def fill_params(
@@ -246,4 +246,11 @@ def lse_merge(o_parts, lse_parts, o_out: torch.Tensor, lse_out: torch.Tensor | N
 
 
 def take_device_error(device_index: int) -> int:
+    """Read and clear the device's sticky kernel status (FA_OK or FA_ERR_TIMEOUT)."""
     return lib.fa_sm100_take_device_error(int(device_index))
+
+
+def set_timeout_ns(ns: int) -> int:
+    """Bound every device-side wait of later launches to `ns` nanoseconds
+    (0 restores the default); returns the previous bound."""
+    return int(lib.fa_sm100_set_timeout_ns(int(ns)))

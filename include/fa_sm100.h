@@ -42,7 +42,7 @@ extern "C" {
 /* Status codes returned by every entry point. */
 #define FA_OK                    0
 #define FA_ERR_INVALID_ARG      -1  /* null pointer, negative size, ...          */
-#define FA_ERR_UNSUPPORTED      -2  /* head_dim not 64/128, heads_k != heads ... */
+#define FA_ERR_UNSUPPORTED      -2  /* head_dim not 64/128, ...                  */
 #define FA_ERR_ALIGNMENT        -3  /* base pointer or stride not 16-byte aligned */
 #define FA_ERR_CUDA             -4  /* a CUDA runtime/driver call failed          */
 #define FA_ERR_NO_DEVICE        -5  /* current device is not an sm_100 part       */
@@ -62,7 +62,8 @@ typedef struct FaParams {
     int32_t seqlen_q;
     int32_t seqlen_k;
     int32_t heads;
-    int32_t heads_k;        /* must equal heads (see flash_api.cpp:29)        */
+    int32_t heads_k;        /* divides heads (flash_api.cpp:29); query head h
+                             * reads K/V head h / (heads / heads_k)          */
     int32_t head_dim;       /* 64 or 128                                      */
 
     int64_t q_batch_stride, q_row_stride, q_head_stride;
@@ -110,6 +111,15 @@ FA_API int fa_sm100_lse_merge(const float *const *o_parts, const float *const *l
  * (synchronises that device).  Returns FA_OK or the recorded error, and
  * clears it. */
 FA_API int fa_sm100_take_device_error(int device);
+
+/* Bound, in nanoseconds, on every device-side wait of later launches from
+ * this process (all devices).  0 restores the default (2 s, or
+ * FA_SM100_TIMEOUT_MS from the environment).  Returns the previous bound.
+ * A bound shorter than the pipeline's own latencies makes the kernel give up
+ * and record FA_ERR_TIMEOUT -- the way to exercise the failure path on a GPU
+ * without faulting it.  No counterpart in the reference (its kernel has no
+ * waits that can expire). */
+FA_API uint64_t fa_sm100_set_timeout_ns(uint64_t ns);
 
 /* Human-readable text for a status code. */
 FA_API const char *fa_sm100_status_string(int status);

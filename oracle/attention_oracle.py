@@ -63,13 +63,16 @@ def math_attention(
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """fp32 attention on the CPU.
 
-    q: (b, sq, h, d), k/v: (b, sk, h, d) in any float dtype (upcast to fp32).
+    q: (b, sq, h, d), k/v: (b, sk, hk, d) in any float dtype (upcast to fp32),
+    hk dividing h: query head hi attends K/V head hi // (h // hk) (GQA/MQA).
     Returns O (b, sq, h, d) fp32 and LSE (b, h, sq) fp32.  Work is chunked
     by (batch, head, query block) so memory stays at q_chunk x sk floats.
     `heads` restricts the computation to a subset of heads (others left 0).
     """
     b, sq, h, d = q.shape
-    sk = k.shape[1]
+    sk, hk = k.shape[1], k.shape[2]
+    assert h % hk == 0, "heads must be divisible by heads_k"
+    group = h // hk
     scale = (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale)
     out = torch.zeros((b, sq, h, d), dtype=torch.float32)
     lse = torch.full((b, h, sq), float("-inf"), dtype=torch.float32)
@@ -81,8 +84,8 @@ def math_attention(
     head_list = range(h) if heads is None else heads
     for bi in range(b):
         for hi in head_list:
-            kk = kf[bi, :, hi, :]
-            vv = vf[bi, :, hi, :]
+            kk = kf[bi, :, hi // group, :]
+            vv = vf[bi, :, hi // group, :]
             for r0 in range(0, sq, q_chunk):
                 r1 = min(sq, r0 + q_chunk)
                 s = (qf[bi, r0:r1, hi, :] @ kk.T) * scale
@@ -168,6 +171,7 @@ def make_inputs(
     seed: int = 0,
     seqlen_k: int | None = None,
     device: str | torch.device = "cpu",
+    heads_k: int | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Seeded i.i.d. N(0,1) q, k, v drawn in fp32 in that order, then cast.
 
@@ -176,9 +180,10 @@ def make_inputs(
     """
     g = torch.Generator(device="cpu").manual_seed(seed)
     sk = seqlen if seqlen_k is None else seqlen_k
+    hk = heads if heads_k is None else heads_k
     q = torch.randn((batch, seqlen, heads, head_dim), generator=g, dtype=torch.float32)
-    k = torch.randn((batch, sk, heads, head_dim), generator=g, dtype=torch.float32)
-    v = torch.randn((batch, sk, heads, head_dim), generator=g, dtype=torch.float32)
+    k = torch.randn((batch, sk, hk, head_dim), generator=g, dtype=torch.float32)
+    v = torch.randn((batch, sk, hk, head_dim), generator=g, dtype=torch.float32)
     return tuple(t.to(dtype).to(device) for t in (q, k, v))
 
 

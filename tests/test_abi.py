@@ -55,7 +55,8 @@ def _params(**kw):
     [
         ({}, 0),
         ({"head_dim": 96}, -2),
-        ({"heads_k": 1}, -2),
+        ({"heads_k": 1}, 0),
+        ({"heads": 4, "heads_k": 3}, -1),
         ({"batch": -1}, -1),
         ({"q": (1 << 20) + 2}, -3),
         ({"q_row_stride": 2 * 64 + 4}, -3),

@@ -29,10 +29,10 @@ def _lse_err(lse, lse_ref):
     return d.max().item() if d.numel() else 0.0
 
 
-def check(b, sq, h, d, dtype, causal, seed=0, sk=None, **oracle_kw):
+def check(b, sq, h, d, dtype, causal, seed=0, sk=None, hk=None, **oracle_kw):
     from flash_attention import flash_attn_func
 
-    q, k, v = make_inputs(b, sq, h, d, dtype, seed=seed, seqlen_k=sk)
+    q, k, v = make_inputs(b, sq, h, d, dtype, seed=seed, seqlen_k=sk, heads_k=hk)
     o, lse = flash_attn_func(q.cuda(), k.cuda(), v.cuda(), causal, return_lse=True)
     torch.cuda.synchronize()
     o_ref, lse_ref = math_attention(q, k, v, causal, **oracle_kw)
@@ -60,6 +60,16 @@ def test_reference_grid(batch, seqlen, head_dim, causal, dtype):
 def test_tails_and_unequal_lengths(sq, sk, causal):
     check(2, sq, 3, 64, torch.bfloat16, causal, seed=sq * 1000 + sk, sk=sk)
     check(1, sq, 2, 128, torch.float16, causal, seed=sq * 1000 + sk + 1, sk=sk)
+
+
+@pytest.mark.parametrize("h,hk", [(8, 2), (8, 1), (6, 3), (4, 4)])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_grouped_query_heads(h, hk, causal, dtype, d):
+    """GQA / MQA: the reference's binding accepts heads % heads_k == 0
+    (flash_api.cpp:29) but its kernel indexes K/V by the query head
+    (kernel.cuh:63,69); here query head i reads K/V head i // (h // hk)."""
+    check(2, 640, h, d, dtype, causal, seed=17, hk=hk)
 
 
 @pytest.mark.parametrize("causal", [False, True])
@@ -101,6 +111,22 @@ def test_position_offsets(q_off, k_off):
     o_ref, lse_ref = math_attention(q, k, v, True, q_pos_offset=q_off, k_pos_offset=k_off)
     assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.bfloat16]
     assert _lse_err(lse, lse_ref) <= LSE_TOL
+
+
+@pytest.mark.parametrize("sq,sk", [(300, 700), (128, 1000), (257, 257)])
+def test_bottom_right_causal(sq, sk):
+    """Bottom-right aligned causal (query i sees keys j <= i + sk - sq, the
+    convention of decoders with a KV cache) through q_pos_offset = sk - sq,
+    against an explicit tril(diagonal = sk - sq) mask."""
+    from flash_attention._C import forward_with_lse
+
+    q, k, v = make_inputs(2, sq, 2, 64, torch.float16, seed=23, seqlen_k=sk)
+    o, _ = forward_with_lse(q.cuda(), k.cuda(), v.cuda(), True, q_pos_offset=sk - sq)
+    qf, kf, vf = (t.float().permute(0, 2, 1, 3) for t in (q, k, v))
+    s = qf @ kf.transpose(-1, -2) / 8.0
+    s = s.masked_fill(~torch.ones(sq, sk, dtype=torch.bool).tril(diagonal=sk - sq), float("-inf"))
+    o_ref = (torch.softmax(s, dim=-1) @ vf).permute(0, 2, 1, 3)
+    assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.float16]
 
 
 def test_empty_inputs():

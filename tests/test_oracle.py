@@ -70,3 +70,14 @@ def test_make_inputs_deterministic():
     b = make_inputs(1, 16, 2, 64, torch.bfloat16, seed=9)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("h,hk", [(8, 2), (6, 1)])
+def test_math_attention_grouped_heads_equal_repeated_kv(h, hk):
+    """GQA in the oracle = plain attention with each K/V head repeated for its
+    group of h // hk query heads."""
+    q, k, v = make_inputs(2, 96, h, 64, torch.float32, seed=3, heads_k=hk)
+    o, lse = math_attention(q, k, v, True)
+    rep = h // hk
+    o2, lse2 = math_attention(q, k.repeat_interleave(rep, dim=2), v.repeat_interleave(rep, dim=2), True)
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)
