@@ -319,6 +319,18 @@ def build_fn(impl, cfg, causal):
     return fn, "reference SM80 kernel (its own csrc, compiled for sm_100a) via _C.forward, O only"
 
 
+def cp_launches(a, b):
+    """Kernel launches of rank 0 per C5 step (attention + LSE-merge kernels)."""
+    if a.gpus == 1:
+        return 1
+    if a.cp_schedule == "gather":
+        return 2
+    world = a.gpus
+    pa, pb = 0, 2 * world - 1
+    attn = 1 + (1 if pa > 0 else 0) + 2 + (1 if pb > world else 0)
+    return attn + 2 * b
+
+
 def run_context_parallel(a, dist_):
     """C5: every rank builds the same seeded full q/k/v, keeps its zigzag
     shard and runs the context-parallel forward (all-gather of K/V + two
@@ -332,8 +344,11 @@ def run_context_parallel(a, dist_):
     if dist_.world > 1:
         q, k, v = (zigzag_shard(t, dist_.world, dist_.rank) for t in (q, k, v))
 
+        overlap = a.cp_schedule == "overlap"
+        workspace = {}
+
         def fn(q_, k_, v_):
-            return context_parallel_attention(q_, k_, v_, True)
+            return context_parallel_attention(q_, k_, v_, True, overlap=overlap, workspace=workspace)
     else:
 
         def fn(q_, k_, v_):
@@ -362,8 +377,13 @@ def run_context_parallel(a, dist_):
                 "workload": f"C5: causal attention b={b} s={s} h={h} d={d} bf16, O + LSE, one sequence over "
                 f"{a.gpus} GPU(s)",
                 "seq_len": s,
-                "parallelism": "zigzag context parallelism: 2N chunks, NCCL all-gather of K and V, "
-                "kernel on global positions" if a.gpus > 1 else "single GPU",
+                "parallelism": (
+                    "zigzag context parallelism: 2N chunks, NCCL all-gather of K and V, kernel on global positions"
+                    + (", gather in two async halves hidden behind local-key compute, fp32 partials LSE-merged"
+                       if a.cp_schedule == "overlap" else ", gather then compute")
+                )
+                if a.gpus > 1
+                else "single GPU",
                 "l2": "inputs larger than L2 (q/k/v = 1 GiB each)",
                 "flops_per_step_total": fl,
             },
@@ -376,7 +396,7 @@ def run_context_parallel(a, dist_):
                 "frac": round(value / a.gpus / peak, 4),
                 "peak_source": f"{peak_src} dense bf16 GEMM (burst)",
             },
-            "gpu_launches": a.steps * (2 if a.gpus > 1 else 1),
+            "gpu_launches": a.steps * cp_launches(a, b),
             "clocks": clocks.summary() if clocks is not None else None,
         }
         print(json.dumps(line), flush=True)
@@ -394,6 +414,9 @@ def main():
     ap.add_argument("--no-variants", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true", help="skip NVML clock sampling")
+    ap.add_argument("--cp-schedule", default="gather", choices=["overlap", "gather"],
+                    help="C5 on N>1 GPUs: gather K/V first (measured faster at N=2), or overlap the gather "
+                    "with compute on the local keys and merge fp32 partials")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 

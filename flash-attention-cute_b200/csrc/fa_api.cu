@@ -214,6 +214,7 @@ int fa_sm100_fwd(const FaParams* p, void* stream_ptr) {
   kp.heads = p->heads;
   kp.batch = p->batch;
   kp.heads_per_kv = p->heads / p->heads_k;
+  kp.o_f32 = p->out_f32 != 0 ? 1 : 0;
   kp.num_m_blocks = (p->seqlen_q + 2 * fa::kBlockM - 1) / (2 * fa::kBlockM);
   kp.scale = p->softmax_scale;
   kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;

@@ -49,6 +49,7 @@ struct FwdKernelParams {
   uint64_t timeout_ns;
   int seqlen_q, seqlen_k, heads, batch;
   int heads_per_kv;  // query heads per K/V head (GQA / MQA group size)
+  int o_f32;         // 1: O is written as fp32 (partial results), else as the input type
   int num_m_blocks;  // ceil(seqlen_q / 256)
   float scale;       // softmax scale
   float scale_log2;  // softmax scale * log2(e)
@@ -574,7 +575,17 @@ __global__ void __launch_bounds__(kThreads, 1) fa_fwd_sm100_kernel(const __grid_
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        if (row_ok) {
+        if (row_ok && p.o_f32) {
+          float* orow32 = reinterpret_cast<float*>(p.o) + static_cast<int64_t>(batch) * p.o_batch_stride +
+                          static_cast<int64_t>(row) * p.o_row_stride +
+                          static_cast<int64_t>(head) * p.o_head_stride + key_half * kHalfD + cc * 32;
+          float4* dst = reinterpret_cast<float4*>(orow32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                 __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+          }
+        } else if (row_ok) {
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {

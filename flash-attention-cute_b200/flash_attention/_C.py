@@ -58,6 +58,7 @@ class FaParams(ctypes.Structure):
         ("q_pos_offset", ctypes.c_int64),
         ("k_pos_offset", ctypes.c_int64),
         ("error_flag", ctypes.c_void_p),
+        ("out_f32", ctypes.c_int32),
     ]
 
 
@@ -174,6 +175,7 @@ def fill_params(
     p.q_pos_offset = int(q_pos_offset)
     p.k_pos_offset = int(k_pos_offset)
     p.error_flag = None
+    p.out_f32 = 1 if o.dtype == torch.float32 else 0
     return p
 
 
@@ -198,6 +200,9 @@ def forward_with_lse(
     lse_out: torch.Tensor | None = None,
 ):
     _validate(q, k, v)
+    if out is not None and (out.shape != q.shape or out.dtype not in (q.dtype, torch.float32)
+                            or out.device != q.device or out.stride(-1) != 1):
+        raise RuntimeError("out must match q's shape and device, with q's dtype or fp32, contiguous in last dim")
     o = torch.empty_like(q) if out is None else out
     lse = None
     if want_lse:

@@ -86,6 +86,11 @@ typedef struct FaParams {
      * inside the kernel expires (the kernel then frees its tensor memory and
      * returns instead of hanging).  NULL: the library's own flag is used. */
     int32_t *error_flag;
+
+    /* 0: o has the input type.  1: o is fp32 (same element strides) -- for
+     * partial results over a subset of the keys that fa_sm100_lse_merge later
+     * combines without an intermediate 16-bit rounding. */
+    int32_t out_f32;
 } FaParams;
 
 /* Validate params without launching anything (host only, no GPU needed). */

@@ -54,23 +54,39 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _oracle_attn(q, k, v, causal, q_pos_offset, out, lse_out):
-    o, lse = math_attention(q, k, v, causal, q_pos_offset=q_pos_offset)
+def _oracle_attn(q, k, v, causal, q_pos_offset, out, lse_out, k_pos_offset=0):
+    o, lse = math_attention(q, k, v, causal, q_pos_offset=q_pos_offset, k_pos_offset=k_pos_offset)
     out.copy_(o.to(out.dtype))
     lse_out.copy_(lse)
 
 
-def _worker(rank, world, port, seqlen, causal, ret):
+def _torch_merge(o_parts, lse_parts, o_out, lse_out):
+    """LSE merge in plain torch (stands in for the merge kernel on CPU)."""
+    lse = torch.stack(lse_parts)  # (n, b, h, c)
+    m = torch.logsumexp(lse, dim=0)
+    w = torch.exp(lse - m)
+    o = sum(w[i].permute(0, 2, 1).unsqueeze(-1) * o_parts[i] for i in range(len(o_parts)))
+    o_out.copy_(o.to(o_out.dtype))
+    lse_out.copy_(m)
+
+
+def _worker(rank, world, port, seqlen, causal, ret, overlap=False, batch=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         torch.manual_seed(0)
-        q, k, v = make_inputs(1, seqlen, 2, 64, torch.float32, seed=21)
+        q, k, v = make_inputs(batch, seqlen, 2, 64, torch.float32, seed=21)
         ql, kl, vl = (zigzag_shard(t, world, rank) for t in (q, k, v))
         # the gathered keys come back in sequence order
         assert torch.equal(gather_zigzag(kl), k)
-        o, lse = context_parallel_attention(ql, kl, vl, causal, attn_fn=_oracle_attn)
+        ws = {}
+        o, lse = context_parallel_attention(ql, kl, vl, causal, attn_fn=_oracle_attn, overlap=overlap,
+                                            merge_fn=_torch_merge, workspace=ws)
+        if overlap:  # a second call reuses the workspace buffers and gives the same result
+            o2, lse2 = context_parallel_attention(ql, kl, vl, causal, attn_fn=_oracle_attn, overlap=True,
+                                                  merge_fn=_torch_merge, workspace=ws)
+            assert torch.equal(o, o2) and torch.equal(lse, lse2) and len(ws) > 0
         outs = [torch.empty_like(o) for _ in range(world)]
         lses = [torch.empty_like(lse) for _ in range(world)]
         dist.all_gather(outs, o)
@@ -88,7 +104,17 @@ def _worker(rank, world, port, seqlen, causal, ret):
 @pytest.mark.parametrize("world,causal", [(2, True), (2, False), (4, True)])
 def test_context_parallel_matches_full_attention(world, causal):
     seqlen = 64 * world
-    ret = mp.Manager().dict()
+    ret = mp.get_context("spawn").Manager().dict()
     mp.start_processes(_worker, args=(world, _free_port(), seqlen, causal, ret), nprocs=world,
+                       start_method="spawn", join=True)
+    assert ret["o_err"] < 1e-5 and ret["lse_err"] < 1e-5, dict(ret)
+
+
+@pytest.mark.parametrize("world,batch", [(2, 1), (4, 1), (4, 2)])
+def test_overlapped_context_parallel_matches_full_attention(world, batch):
+    """Gather in two asynchronous halves, partial results merged by LSE."""
+    seqlen = 64 * world
+    ret = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_worker, args=(world, _free_port(), seqlen, True, ret, True, batch), nprocs=world,
                        start_method="spawn", join=True)
     assert ret["o_err"] < 1e-5 and ret["lse_err"] < 1e-5, dict(ret)

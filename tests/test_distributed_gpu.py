@@ -48,7 +48,7 @@ def _free_port():
         return sck.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, ret):
+def _nccl_worker(rank, world, port, ret, overlap=False):
     import datetime
 
     import torch.distributed as dist
@@ -64,7 +64,7 @@ def _nccl_worker(rank, world, port, ret):
         s = 2048
         q, k, v = make_inputs(1, s, 2, 128, torch.bfloat16, seed=41)
         ql, kl, vl = (zigzag_shard(t, world, rank).cuda() for t in (q, k, v))
-        o, lse = context_parallel_attention(ql, kl, vl, True)
+        o, lse = context_parallel_attention(ql, kl, vl, True, overlap=overlap)
         outs = [torch.empty_like(o) for _ in range(world)]
         lses = [torch.empty_like(lse) for _ in range(world)]
         dist.all_gather(outs, o)
@@ -80,10 +80,22 @@ def _nccl_worker(rank, world, port, ret):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_cp_nccl():
+def _run_nccl(world, overlap):
     import torch.multiprocessing as mp
 
-    ret = mp.Manager().dict()
-    mp.start_processes(_nccl_worker, args=(2, _free_port(), ret), nprocs=2, start_method="spawn", join=True)
+    ret = mp.get_context("spawn").Manager().dict()
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), ret, overlap), nprocs=world, start_method="spawn",
+                       join=True)
     assert ret["o_err"] <= O_TOL[torch.bfloat16] and ret["lse_err"] <= 1e-3, dict(ret)
+
+
+def test_cp_overlapped_single_rank():
+    """The overlapped schedule (async NCCL gathers, fp32 partials, merge
+    kernel) on a one-rank group, so a one-GPU box exercises it too."""
+    _run_nccl(1, True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("overlap", [False, True])
+def test_cp_nccl(overlap):
+    _run_nccl(2, overlap)

@@ -129,6 +129,33 @@ def test_bottom_right_causal(sq, sk):
     assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.float16]
 
 
+@pytest.mark.parametrize("dtype,causal", [(torch.bfloat16, False), (torch.float16, True)])
+def test_fp32_partials_merge_to_full_attention(dtype, causal):
+    """fp32 partial outputs over disjoint key ranges (out_f32), combined by
+    the LSE-merge kernel, equal attention over all keys."""
+    from flash_attention._C import forward_with_lse, lse_merge
+
+    sq, sk, h, d = 700, 3000, 4, 128
+    q, k, v = make_inputs(1, sq, h, d, dtype, seed=29, seqlen_k=sk)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    q_off = sk - sq  # causal: bottom-right aligned, every row sees >= 1 key of every range
+    o_parts, l_parts = [], []
+    for k0, k1 in ((0, 1100), (1100, 2048), (2048, sk)):
+        o = torch.empty((1, sq, h, d), dtype=torch.float32, device="cuda")
+        lse = torch.empty((1, h, sq), dtype=torch.float32, device="cuda")
+        forward_with_lse(qd, kd[:, k0:k1], vd[:, k0:k1], causal, q_pos_offset=q_off, k_pos_offset=k0,
+                         out=o, lse_out=lse)
+        o_parts.append(o[0])
+        l_parts.append(lse[0])
+    o_m = torch.empty((sq, h, d), dtype=dtype, device="cuda")
+    l_m = torch.empty((h, sq), dtype=torch.float32, device="cuda")
+    lse_merge(o_parts, l_parts, o_m, l_m)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = math_attention(q, k, v, causal, q_pos_offset=q_off)
+    assert (o_m.float().cpu() - o_ref[0]).abs().max() <= O_TOL[dtype]
+    assert (l_m.cpu() - lse_ref[0]).abs().max() <= LSE_TOL
+
+
 def test_empty_inputs():
     from flash_attention import flash_attn_func
 
