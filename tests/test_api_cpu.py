@@ -30,5 +30,18 @@ def test_module_layout_matches_reference():
     from flash_attention import _C
     from flash_attention.interface import flash_attn_func as f2
 
-    assert flash_attention.__all__ == ["flash_attn_func"]
+    # the reference's one export first; the host-streaming call is an addition
+    assert flash_attention.__all__[0] == "flash_attn_func"
+    assert set(flash_attention.__all__) == {"flash_attn_func", "flash_attn_func_host"}
     assert callable(_C.forward) and f2 is flash_attn_func
+
+
+def test_host_streaming_rejects_unpinned_tensors():
+    from flash_attention import flash_attn_func_host
+
+    x = torch.zeros(1, 8, 2, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="pinned host memory"):
+        flash_attn_func_host(x, x, x)
+    with pytest.raises(RuntimeError, match="contiguous"):
+        y = torch.zeros(1, 8, 2, 128, dtype=torch.float16)[..., ::2]
+        flash_attn_func_host(y, y, y)
