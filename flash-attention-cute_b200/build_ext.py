@@ -24,6 +24,9 @@ LIB_NAME = "libfa_sm100.so"
 LIB_PATH = os.path.join(PKG, LIB_NAME)
 
 MAIN_SOURCE = os.path.join(CSRC, "fa_api.cu")
+# the allocation-free split entry point (its own translation unit: it owns a
+# static device scratch array and calls the public entry points above)
+NOALLOC_SOURCE = os.path.join(CSRC, "fa_noalloc.cu")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
     "-O3",
@@ -63,7 +66,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     if not force and up_to_date():
         return LIB_PATH
     tmp = LIB_PATH + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, *(extra_flags or []), f"-I{INCLUDE}", f"-I{CSRC}", "-o", tmp, MAIN_SOURCE]
+    cmd = [_nvcc(), *NVCC_FLAGS, *(extra_flags or []), f"-I{INCLUDE}", f"-I{CSRC}", "-o", tmp, MAIN_SOURCE, NOALLOC_SOURCE]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

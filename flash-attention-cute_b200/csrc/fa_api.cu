@@ -277,6 +277,9 @@ const char* fa_sm100_status_string(int status) {
     case FA_ERR_CUDA: return "CUDA error";
     case FA_ERR_NO_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case FA_ERR_TIMEOUT: return "device-side wait timed out";
+    case FA_ERR_SCRATCH_LIMIT:
+      return "problem exceeds the fixed no-alloc scratch (splits x batch x seqlen_q x heads x (head_dim + 1) x 4 "
+             "bytes > fa_sm100_split_scratch_bytes())";
     default: return "unknown status";
   }
 }

@@ -27,6 +27,7 @@
 #ifndef FA_SM100_H_
 #define FA_SM100_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -47,6 +48,8 @@ extern "C" {
 #define FA_ERR_CUDA             -4  /* a CUDA runtime/driver call failed          */
 #define FA_ERR_NO_DEVICE        -5  /* current device is not an sm_100 part       */
 #define FA_ERR_TIMEOUT          -6  /* a bounded device wait ran out (see below)  */
+#define FA_ERR_SCRATCH_LIMIT    -7  /* problem larger than the fixed scratch of
+                                       fa_sm100_fwd_split_noalloc                 */
 
 /* Launch parameters.  Strides are in ELEMENTS (not bytes), like
  * flash::ForwardParams (csrc/flash.h:21-36).  Layout is BSHD:
@@ -125,6 +128,28 @@ FA_API int fa_sm100_take_device_error(int device);
  * without faulting it.  No counterpart in the reference (its kernel has no
  * waits that can expire). */
 FA_API uint64_t fa_sm100_set_timeout_ns(uint64_t ns);
+
+/* Attention forward for callers that cannot allocate device memory (an
+ * engine whose memory pool owns the whole GPU, a loop where an allocation and
+ * the synchronisation it can cause are not allowed, a C/FFI caller holding
+ * only its own tensor pointers).  Same inputs, outputs and result as
+ * fa_sm100_fwd, but the keys are processed in n_splits (1..16) contiguous
+ * ranges whose fp32 partial O and LSE live in a scratch array the library
+ * reserves on every GPU that loads it (fa_sm100_split_scratch_bytes(), 64 MiB,
+ * held until the process exits); the parts are then LSE-merged into p->o /
+ * p->lse.  Nothing is allocated.
+ * Limits: parts * batch * seqlen_q * heads * 4 * (head_dim + 1) bytes must fit
+ * the scratch (else FA_ERR_SCRATCH_LIMIT, nothing launched); p->out_f32 must
+ * be 0 and, when p->lse is set, its head stride must equal seqlen_q
+ * (else FA_ERR_UNSUPPORTED).  The first call on a device looks up the
+ * scratch's device address; make that first call before any stream capture.
+ * All calls share one scratch array: calls that can overlap on the GPU (two
+ * streams, two host threads) race on it and must be serialised by the
+ * caller.  No counterpart in the reference. */
+FA_API int fa_sm100_fwd_split_noalloc(const FaParams *p, int32_t n_splits, void *stream);
+
+/* Size in bytes of the scratch array fa_sm100_fwd_split_noalloc uses. */
+FA_API size_t fa_sm100_split_scratch_bytes(void);
 
 /* Human-readable text for a status code. */
 FA_API const char *fa_sm100_status_string(int status);
