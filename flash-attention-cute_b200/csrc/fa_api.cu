@@ -76,7 +76,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // TMA descriptor over a BSHD operand viewed as 4-D (d, head, seq, batch) with
 // a (64, 1, 128, 1) box and 128-byte swizzle: one box is 128 rows of 128
 // bytes, exactly the canonical K-major / MN-major SW128 UMMA atom stack.
-int encode_operand(CUtensorMap* m, const void* base, bool bf16, int head_dim, int64_t seqlen,
+int encode_operand_uncached(CUtensorMap* m, const void* base, bool bf16, int head_dim, int64_t seqlen,
                    int64_t heads, int64_t batch, int64_t row_stride, int64_t head_stride,
                    int64_t batch_stride) {
   auto fn = encode_fn();
@@ -96,6 +96,51 @@ int encode_operand(CUtensorMap* m, const void* base, bool bf16, int head_dim, in
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? FA_OK : FA_ERR_UNSUPPORTED;
+}
+
+// Encoding a descriptor costs about as much host time as the launch itself,
+// and callers in a loop pass the same tensors again and again: keep the last
+// few descriptors per host thread, keyed by every input of the encoding (a
+// descriptor depends only on the address, shape, strides and box, never on
+// the memory's contents).
+struct TmapKey {
+  const void* base;
+  int64_t seqlen, heads, batch, row_stride, head_stride, batch_stride;
+  int head_dim, bf16;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && seqlen == o.seqlen && heads == o.heads && batch == o.batch &&
+           row_stride == o.row_stride && head_stride == o.head_stride && batch_stride == o.batch_stride &&
+           head_dim == o.head_dim && bf16 == o.bf16;
+  }
+};
+struct TmapCache {
+  static constexpr int kEntries = 16;
+  TmapKey key[kEntries];
+  CUtensorMap map[kEntries];
+  bool valid[kEntries] = {};
+  int next = 0;
+};
+
+int encode_operand(CUtensorMap* m, const void* base, bool bf16, int head_dim, int64_t seqlen, int64_t heads,
+                   int64_t batch, int64_t row_stride, int64_t head_stride, int64_t batch_stride) {
+  thread_local TmapCache cache;
+  const TmapKey k{base, seqlen, heads, batch, row_stride, head_stride, batch_stride, head_dim, bf16 ? 1 : 0};
+  for (int i = 0; i < TmapCache::kEntries; ++i) {
+    if (cache.valid[i] && cache.key[i] == k) {
+      std::memcpy(m, &cache.map[i], sizeof(CUtensorMap));
+      return FA_OK;
+    }
+  }
+  const int rc = encode_operand_uncached(m, base, bf16, head_dim, seqlen, heads, batch, row_stride, head_stride,
+                                         batch_stride);
+  if (rc == FA_OK) {
+    const int i = cache.next;
+    cache.next = (i + 1) % TmapCache::kEntries;
+    cache.key[i] = k;
+    std::memcpy(&cache.map[i], m, sizeof(CUtensorMap));
+    cache.valid[i] = true;
+  }
+  return rc;
 }
 
 // Bound on any single device-side wait.  FA_SM100_TIMEOUT_MS overrides the
@@ -121,9 +166,16 @@ template <int D, bool BF16, bool CAUSAL, bool DIAG>
 int launch(const fa::FwdKernelParams& kp, cudaStream_t stream) {
   using Tr = fa::FwdTraits<D>;
   auto kernel = fa::fa_fwd_sm100_kernel<D, BF16, CAUSAL, DIAG>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
-  if (e != cudaSuccess) return FA_ERR_CUDA;
+  // The shared-memory opt-in is set once per device for each instantiation.
+  static std::atomic<bool> configured[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA_ERR_CUDA;
+  cudaError_t e = cudaSuccess;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+    if (e != cudaSuccess) return FA_ERR_CUDA;
+    configured[dev].store(true, std::memory_order_release);
+  }
   const int64_t grid = static_cast<int64_t>(kp.num_m_blocks) * kp.heads * kp.batch;
   if (grid <= 0 || grid > 0x7fffffffLL) return FA_ERR_UNSUPPORTED;
   kernel<<<static_cast<unsigned>(grid), fa::kThreads, Tr::kSmemBytes, stream>>>(kp);

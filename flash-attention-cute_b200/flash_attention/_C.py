@@ -15,6 +15,7 @@ from __future__ import annotations
 import ctypes
 import math
 import os
+import struct
 
 import torch
 
@@ -108,6 +109,23 @@ def _load() -> ctypes.CDLL:
 
 lib = _load()
 
+# Fast launch path: FaParams packed with one struct.pack call (layout checked
+# against the ctypes mirror below) and passed as a byte buffer.  For small
+# problems the per-call host cost is comparable to the kernel itself.
+_PACKED = struct.Struct("=5Q6i14qf2i4x2qQi4x")
+_fwd_packed = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_char_p, ctypes.c_void_p)(("fa_sm100_fwd", lib))
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _check_packed_layout() -> None:
+    vals = (1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, *range(12, 26), 0.5, 1, 1, 26, 27, 28, 1)
+    mirror = FaParams(*vals)
+    if _PACKED.size != ctypes.sizeof(FaParams) or _PACKED.pack(*vals) != bytes(mirror):
+        raise ImportError("packed FaParams layout does not match the ctypes mirror")
+
+
+_check_packed_layout()
+
 
 def status_string(rc: int) -> str:
     return lib.fa_sm100_status_string(rc).decode()
@@ -158,32 +176,35 @@ def fill_params(
     q_pos_offset: int = 0,
     k_pos_offset: int = 0,
 ) -> FaParams:
-    p = FaParams()
-    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
-    p.lse = lse.data_ptr() if lse is not None else None
-    p.batch, p.seqlen_q, p.heads, p.head_dim = q.shape
-    p.seqlen_k, p.heads_k = k.size(1), k.size(2)
-    p.q_batch_stride, p.q_row_stride, p.q_head_stride = q.stride(0), q.stride(1), q.stride(2)
-    p.k_batch_stride, p.k_row_stride, p.k_head_stride = k.stride(0), k.stride(1), k.stride(2)
-    p.v_batch_stride, p.v_row_stride, p.v_head_stride = v.stride(0), v.stride(1), v.stride(2)
-    p.o_batch_stride, p.o_row_stride, p.o_head_stride = o.stride(0), o.stride(1), o.stride(2)
-    if lse is not None:
-        p.lse_batch_stride, p.lse_head_stride = lse.stride(0), lse.stride(1)
-    p.softmax_scale = (1.0 / math.sqrt(q.size(3))) if softmax_scale is None else float(softmax_scale)
-    p.is_causal = 1 if causal else 0
-    p.is_bf16 = 1 if q.dtype == torch.bfloat16 else 0
-    p.q_pos_offset = int(q_pos_offset)
-    p.k_pos_offset = int(k_pos_offset)
-    p.error_flag = None
-    p.out_f32 = 1 if o.dtype == torch.float32 else 0
-    return p
+    # One positional constructor call (field order of struct FaParams): the
+    # per-call host cost matters for small problems.
+    b, sq, h, d = q.shape
+    qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), o.stride()
+    ls = lse.stride() if lse is not None else (0, 0, 0)
+    return FaParams(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if lse is not None else None,
+        b, sq, k.shape[1], h, k.shape[2], d,
+        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2],
+        ls[0], ls[1],
+        (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale),
+        1 if causal else 0,
+        1 if q.dtype == torch.bfloat16 else 0,
+        int(q_pos_offset),
+        int(k_pos_offset),
+        None,
+        1 if o.dtype == torch.float32 else 0,
+    )
 
 
 def launch(p: FaParams, device: torch.device) -> None:
     """Enqueue the kernel for filled params on the current stream of `device`."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        stream = torch.cuda.current_stream().cuda_stream
+        _check(lib.fa_sm100_fwd(ctypes.byref(p), stream), "fa_sm100_fwd")
+        return
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        _check(lib.fa_sm100_fwd(ctypes.byref(p), ctypes.c_void_p(stream)), "fa_sm100_fwd")
+        _check(lib.fa_sm100_fwd(ctypes.byref(p), stream), "fa_sm100_fwd")
 
 
 def forward_with_lse(
@@ -203,16 +224,30 @@ def forward_with_lse(
     if out is not None and (out.shape != q.shape or out.dtype not in (q.dtype, torch.float32)
                             or out.device != q.device or out.stride(-1) != 1):
         raise RuntimeError("out must match q's shape and device, with q's dtype or fp32, contiguous in last dim")
+    b, sq, h, d = q.shape
     o = torch.empty_like(q) if out is None else out
     lse = None
     if want_lse:
-        lse = (
-            torch.empty((q.size(0), q.size(2), q.size(1)), dtype=torch.float32, device=q.device)
-            if lse_out is None
-            else lse_out
-        )
-    p = fill_params(q, k, v, o, lse, causal, softmax_scale, q_pos_offset, k_pos_offset)
-    launch(p, q.device)
+        lse = q.new_empty((b, h, sq), dtype=torch.float32) if lse_out is None else lse_out
+    qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), o.stride()
+    ls = lse.stride() if lse is not None else (0, 0, 0)
+    packed = _PACKED.pack(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if lse is not None else 0,
+        b, sq, k.shape[1], h, k.shape[2], d,
+        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2], ls[0], ls[1],
+        (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale),
+        1 if causal else 0,
+        1 if q.dtype == torch.bfloat16 else 0,
+        int(q_pos_offset), int(k_pos_offset), 0,
+        1 if o.dtype == torch.float32 else 0,
+    )
+    idx = q.device.index
+    if idx == torch.cuda.current_device():
+        stream = _raw_stream(idx) if _raw_stream is not None else torch.cuda.current_stream().cuda_stream
+        _check(_fwd_packed(packed, stream), "fa_sm100_fwd")
+    else:
+        with torch.cuda.device(q.device):
+            _check(_fwd_packed(packed, torch.cuda.current_stream(q.device).cuda_stream), "fa_sm100_fwd")
     return o, lse
 
 

@@ -156,6 +156,25 @@ def test_fp32_partials_merge_to_full_attention(dtype, causal):
     assert (l_m.cpu() - lse_ref[0]).abs().max() <= LSE_TOL
 
 
+def test_repeated_and_alternating_tensors():
+    """The launcher keeps recent TMA descriptors per host thread, keyed by
+    address, shape and strides: alternating between tensors of one shape, and
+    views of the same storage with other strides, must each get their own."""
+    from flash_attention import flash_attn_func
+
+    a = make_inputs(2, 384, 4, 64, torch.float16, seed=61)
+    b = make_inputs(2, 384, 4, 64, torch.float16, seed=62)
+    ad, bd = [t.cuda() for t in a], [t.cuda() for t in b]
+    refs = {n: math_attention(*x, False)[0] for n, x in (("a", a), ("b", b))}
+    for n in "abab":
+        o = flash_attn_func(*(ad if n == "a" else bd), False)
+        assert (o.float().cpu() - refs[n]).abs().max() <= O_TOL[torch.float16]
+    # same storage seen as BHSD-contiguous then re-viewed as BSHD: new strides
+    qt = ad[0].transpose(1, 2).contiguous().transpose(1, 2)
+    o = flash_attn_func(qt, ad[1], ad[2], False)
+    assert (o.float().cpu() - refs["a"]).abs().max() <= O_TOL[torch.float16]
+
+
 def test_empty_inputs():
     from flash_attention import flash_attn_func
 
