@@ -19,6 +19,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "fa_bwd_sm100.cuh"
 #include "fa_fwd_sm100.cuh"
 #include "fa_lse_merge.cuh"
 #include "fa_sm100.h"
@@ -195,6 +196,90 @@ int launch_causal(const fa::FwdKernelParams& kp, bool causal, cudaStream_t s) {
   return causal ? launch<D, BF16, true, false>(kp, s) : launch<D, BF16, false, false>(kp, s);
 }
 
+
+// ---------------------------------------------------------------- backward
+template <typename K>
+int set_smem_once(K kernel, int bytes, std::atomic<bool>* configured) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA_ERR_CUDA;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+      return FA_ERR_CUDA;
+    }
+    configured[dev].store(true, std::memory_order_release);
+  }
+  return FA_OK;
+}
+
+template <int D, bool BF16, bool CAUSAL>
+int launch_bwd(const fa::BwdKernelParams& kp, const FaBwdParams* p, cudaStream_t stream) {
+  // D = rowsum(dO * O): one warp per (batch, head, row)
+  const int64_t rows = static_cast<int64_t>(p->batch) * p->heads * p->seqlen_q;
+  const int64_t dot_blocks = (rows + 7) / 8;
+  if (dot_blocks > 0x7fffffffLL) return FA_ERR_UNSUPPORTED;
+  fa::fa_bwd_dot_kernel<D, BF16><<<static_cast<unsigned>(dot_blocks), 256, 0, stream>>>(
+      p->dout, p->o, p->dvec, p->batch, p->seqlen_q, p->heads, p->do_batch_stride, p->do_row_stride,
+      p->do_head_stride, p->o_batch_stride, p->o_row_stride, p->o_head_stride);
+  if (cudaGetLastError() != cudaSuccess) return FA_ERR_CUDA;
+
+  static std::atomic<bool> cfg_dq[kMaxDevices];
+  static std::atomic<bool> cfg_kv[kMaxDevices];
+  auto dq_kernel = fa::fa_bwd_dq_kernel<D, BF16, CAUSAL>;
+  auto kv_kernel = fa::fa_bwd_dkdv_kernel<D, BF16, CAUSAL>;
+  int rc = set_smem_once(dq_kernel, fa::BwdTraits<D>::kSmemBytes, cfg_dq);
+  if (rc != FA_OK) return rc;
+  rc = set_smem_once(kv_kernel, fa::BwdKVTraits<D>::kSmemBytes, cfg_kv);
+  if (rc != FA_OK) return rc;
+  const int64_t grid_q = static_cast<int64_t>(kp.num_q_blocks) * kp.heads * kp.batch;
+  const int64_t grid_k = static_cast<int64_t>(kp.num_k_blocks) * kp.heads_k * kp.batch;
+  if (grid_q > 0x7fffffffLL || grid_k > 0x7fffffffLL) return FA_ERR_UNSUPPORTED;
+  if (grid_q > 0) {
+    dq_kernel<<<static_cast<unsigned>(grid_q), fa::kThreads, fa::BwdTraits<D>::kSmemBytes, stream>>>(kp);
+    if (cudaGetLastError() != cudaSuccess) return FA_ERR_CUDA;
+  }
+  if (grid_k > 0) {
+    kv_kernel<<<static_cast<unsigned>(grid_k), fa::kThreads, fa::BwdKVTraits<D>::kSmemBytes, stream>>>(kp);
+    if (cudaGetLastError() != cudaSuccess) return FA_ERR_CUDA;
+  }
+  return FA_OK;
+}
+
+template <int D, bool BF16>
+int launch_bwd_causal(const fa::BwdKernelParams& kp, const FaBwdParams* p, cudaStream_t s) {
+  return p->is_causal ? launch_bwd<D, BF16, true>(kp, p, s) : launch_bwd<D, BF16, false>(kp, p, s);
+}
+
+int check_bwd_params(const FaBwdParams* p) {
+  if (p == nullptr) return FA_ERR_INVALID_ARG;
+  if (p->batch < 0 || p->seqlen_q < 0 || p->seqlen_k < 0 || p->heads <= 0 || p->heads_k <= 0) {
+    return FA_ERR_INVALID_ARG;
+  }
+  if (p->head_dim != 64 && p->head_dim != 128) return FA_ERR_UNSUPPORTED;
+  if (p->heads % p->heads_k != 0) return FA_ERR_INVALID_ARG;
+  if (!std::isfinite(p->softmax_scale)) return FA_ERR_INVALID_ARG;
+  if (p->batch == 0 || (p->seqlen_q == 0 && p->seqlen_k == 0)) return FA_OK;
+  const void* ptrs[] = {p->q, p->k, p->v, p->o, p->dout, p->dq, p->dk, p->dv};
+  for (const void* q : ptrs) {
+    if (q == nullptr) return FA_ERR_INVALID_ARG;
+    if (!aligned16(q)) return FA_ERR_ALIGNMENT;
+  }
+  if (p->lse == nullptr || p->dvec == nullptr) return FA_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(p->lse) & 3u) || (reinterpret_cast<uintptr_t>(p->dvec) & 3u)) {
+    return FA_ERR_ALIGNMENT;
+  }
+  const int64_t st[] = {p->q_batch_stride,  p->q_row_stride,  p->q_head_stride,  p->k_batch_stride,
+                        p->k_row_stride,    p->k_head_stride, p->v_batch_stride, p->v_row_stride,
+                        p->v_head_stride,   p->o_batch_stride, p->o_row_stride,  p->o_head_stride,
+                        p->do_batch_stride, p->do_row_stride, p->do_head_stride, p->dq_batch_stride,
+                        p->dq_row_stride,   p->dq_head_stride, p->dk_batch_stride, p->dk_row_stride,
+                        p->dk_head_stride,  p->dv_batch_stride, p->dv_row_stride, p->dv_head_stride};
+  for (int64_t s : st) {
+    if (!stride_ok(s)) return FA_ERR_ALIGNMENT;
+  }
+  if (p->lse_batch_stride < 0 || p->lse_head_stride < 0) return FA_ERR_INVALID_ARG;
+  return FA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -347,6 +432,96 @@ int fa_sm100_num_sms(int device) {
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
   return n;
+}
+
+int fa_sm100_bwd_params_size(void) { return static_cast<int>(sizeof(FaBwdParams)); }
+
+int fa_sm100_bwd(const FaBwdParams* p, void* stream_ptr) {
+  int rc = check_bwd_params(p);
+  if (rc != FA_OK) return rc;
+  if (p->batch == 0 || (p->seqlen_q == 0 && p->seqlen_k == 0)) return FA_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  DeviceState* ds = nullptr;
+  rc = device_state(dev, &ds);
+  if (rc != FA_OK) return rc;
+  if (ds->sm_major != 10) return FA_ERR_NO_DEVICE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream_ptr);
+  const bool bf16 = p->is_bf16 != 0;
+  const int64_t b = p->batch, sq = p->seqlen_q, sk = p->seqlen_k, d = p->head_dim;
+  // Empty key set: dQ = 0; empty query set: dK = dV = 0 (plain memsets).
+  if (sk == 0 || sq == 0) {
+    auto zero = [&](void* ptr, int64_t rows, int64_t heads, int64_t bs, int64_t rs, int64_t hs) {
+      for (int64_t bi = 0; bi < b; ++bi) {
+        for (int64_t r = 0; r < rows; ++r) {
+          char* base = static_cast<char*>(ptr) + 2 * (bi * bs + r * rs);
+          if (hs == d) {
+            if (cudaMemsetAsync(base, 0, static_cast<size_t>(2 * heads * d), s) != cudaSuccess) return false;
+          } else {
+            for (int64_t h = 0; h < heads; ++h) {
+              if (cudaMemsetAsync(base + 2 * h * hs, 0, static_cast<size_t>(2 * d), s) != cudaSuccess) return false;
+            }
+          }
+        }
+      }
+      return true;
+    };
+    const bool ok = sk == 0 ? zero(p->dq, sq, p->heads, p->dq_batch_stride, p->dq_row_stride, p->dq_head_stride)
+                            : (zero(p->dk, sk, p->heads_k, p->dk_batch_stride, p->dk_row_stride, p->dk_head_stride) &&
+                               zero(p->dv, sk, p->heads_k, p->dv_batch_stride, p->dv_row_stride, p->dv_head_stride));
+    return ok ? FA_OK : FA_ERR_CUDA;
+  }
+  fa::BwdKernelParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  rc = encode_operand(&kp.tm_q, p->q, bf16, p->head_dim, sq, p->heads, b, p->q_row_stride, p->q_head_stride,
+                      p->q_batch_stride);
+  if (rc == FA_OK) {
+    rc = encode_operand(&kp.tm_do, p->dout, bf16, p->head_dim, sq, p->heads, b, p->do_row_stride,
+                        p->do_head_stride, p->do_batch_stride);
+  }
+  if (rc == FA_OK) {
+    rc = encode_operand(&kp.tm_k, p->k, bf16, p->head_dim, sk, p->heads_k, b, p->k_row_stride, p->k_head_stride,
+                        p->k_batch_stride);
+  }
+  if (rc == FA_OK) {
+    rc = encode_operand(&kp.tm_v, p->v, bf16, p->head_dim, sk, p->heads_k, b, p->v_row_stride, p->v_head_stride,
+                        p->v_batch_stride);
+  }
+  if (rc != FA_OK) return rc;
+  kp.lse = p->lse;
+  kp.dvec = p->dvec;
+  kp.dq = p->dq;
+  kp.dk = p->dk;
+  kp.dv = p->dv;
+  kp.error_flag = p->error_flag != nullptr ? p->error_flag : ds->error_flag;
+  kp.dq_batch_stride = p->dq_batch_stride;
+  kp.dq_row_stride = p->dq_row_stride;
+  kp.dq_head_stride = p->dq_head_stride;
+  kp.dk_batch_stride = p->dk_batch_stride;
+  kp.dk_row_stride = p->dk_row_stride;
+  kp.dk_head_stride = p->dk_head_stride;
+  kp.dv_batch_stride = p->dv_batch_stride;
+  kp.dv_row_stride = p->dv_row_stride;
+  kp.dv_head_stride = p->dv_head_stride;
+  kp.lse_batch_stride = p->lse_batch_stride;
+  kp.lse_head_stride = p->lse_head_stride;
+  kp.q_pos_offset = p->q_pos_offset;
+  kp.k_pos_offset = p->k_pos_offset;
+  kp.timeout_ns = timeout_ns() < kDiagBoundNs ? kDiagBoundNs : timeout_ns();
+  kp.seqlen_q = p->seqlen_q;
+  kp.seqlen_k = p->seqlen_k;
+  kp.heads = p->heads;
+  kp.heads_k = p->heads_k;
+  kp.batch = p->batch;
+  kp.heads_per_kv = p->heads / p->heads_k;
+  kp.num_q_blocks = static_cast<int>((sq + fa::kBlockM - 1) / fa::kBlockM);
+  kp.num_k_blocks = static_cast<int>((sk + fa::kBlockN - 1) / fa::kBlockN);
+  kp.scale = p->softmax_scale;
+  kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  if (p->head_dim == 64) {
+    return bf16 ? launch_bwd_causal<64, true>(kp, p, s) : launch_bwd_causal<64, false>(kp, p, s);
+  }
+  return bf16 ? launch_bwd_causal<128, true>(kp, p, s) : launch_bwd_causal<128, false>(kp, p, s);
 }
 
 }  // extern "C"

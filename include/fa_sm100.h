@@ -151,6 +151,43 @@ FA_API int fa_sm100_fwd_split_noalloc(const FaParams *p, int32_t n_splits, void 
 /* Size in bytes of the scratch array fa_sm100_fwd_split_noalloc uses. */
 FA_API size_t fa_sm100_split_scratch_bytes(void);
 
+/* Backward pass: gradients dQ, dK, dV of O = attention(Q, K, V) given dO and
+ * the forward's O and LSE (no counterpart in the reference, which has no
+ * backward).  Layout, dtypes, head_dim, GQA, causal convention and position
+ * offsets are those of FaParams.  `dvec` is caller-provided scratch of
+ * batch * heads * seqlen_q floats (D = rowsum(dO * O)); dq/dk/dv are written
+ * in the input type.  Deterministic: no atomics. */
+typedef struct FaBwdParams {
+    const void  *q, *k, *v, *o, *dout;
+    const float *lse;       /* (batch, heads, seqlen_q), row stride 1        */
+    void        *dq, *dk, *dv;
+    float       *dvec;      /* scratch, batch * heads * seqlen_q floats      */
+
+    int32_t batch, seqlen_q, seqlen_k, heads, heads_k, head_dim;
+
+    int64_t q_batch_stride, q_row_stride, q_head_stride;
+    int64_t k_batch_stride, k_row_stride, k_head_stride;
+    int64_t v_batch_stride, v_row_stride, v_head_stride;
+    int64_t o_batch_stride, o_row_stride, o_head_stride;
+    int64_t do_batch_stride, do_row_stride, do_head_stride;
+    int64_t dq_batch_stride, dq_row_stride, dq_head_stride;
+    int64_t dk_batch_stride, dk_row_stride, dk_head_stride;
+    int64_t dv_batch_stride, dv_row_stride, dv_head_stride;
+    int64_t lse_batch_stride, lse_head_stride;
+
+    float   softmax_scale;
+    int32_t is_causal;
+    int32_t is_bf16;
+    int64_t q_pos_offset;
+    int64_t k_pos_offset;
+    int32_t *error_flag;    /* as FaParams.error_flag                         */
+} FaBwdParams;
+
+FA_API int fa_sm100_bwd(const FaBwdParams *p, void *stream);
+
+/* sizeof(FaBwdParams) as compiled into the library. */
+FA_API int fa_sm100_bwd_params_size(void);
+
 /* Human-readable text for a status code. */
 FA_API const char *fa_sm100_status_string(int status);
 

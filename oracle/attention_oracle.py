@@ -101,6 +101,41 @@ def math_attention(
     return out, lse
 
 
+def math_attention_backward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    dout: torch.Tensor,
+    causal: bool = False,
+    softmax_scale: float | None = None,
+    q_pos_offset: int = 0,
+    k_pos_offset: int = 0,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """fp32 gradients (dq, dk, dv) of softmax(scale Q K^T [+ mask]) V on the
+    CPU by torch autograd, for the backward's parity tests.  K/V heads are
+    shared by groups of query heads (GQA) exactly as in math_attention; rows
+    with no visible key contribute nothing."""
+    b, sq, h, d = q.shape
+    hk = k.shape[2]
+    group = h // hk
+    scale = (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale)
+    qf = q.detach().to("cpu", torch.float32).requires_grad_(True)
+    kf = k.detach().to("cpu", torch.float32).requires_grad_(True)
+    vf = v.detach().to("cpu", torch.float32).requires_grad_(True)
+    kr = kf.repeat_interleave(group, dim=2).permute(0, 2, 1, 3)
+    vr = vf.repeat_interleave(group, dim=2).permute(0, 2, 1, 3)
+    s = (qf.permute(0, 2, 1, 3) @ kr.transpose(-1, -2)) * scale
+    if causal:
+        vis = _visible_mask(sq, k.shape[1], q_pos_offset, k_pos_offset)
+        s = s.masked_fill(~vis, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1, keepdim=True)
+    p = torch.where(torch.isfinite(lse), torch.exp(s - torch.where(torch.isfinite(lse), lse, torch.zeros_like(lse))),
+                    torch.zeros_like(s))
+    o = (p @ vr).permute(0, 2, 1, 3)
+    o.backward(dout.detach().to("cpu", torch.float32))
+    return qf.grad, kf.grad, vf.grad
+
+
 def tiled_reference_algorithm(
     q: np.ndarray | torch.Tensor,
     k: np.ndarray | torch.Tensor,
