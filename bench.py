@@ -499,6 +499,25 @@ def main():
             "roofline_frac": round(fl_c / (launch_c * 1e-3) / 1e12 / peak, 4),
         }
 
+    if not a.no_variants and a.impl == "ours" and a.config in ("C2", "C3", "C4", "C4s"):
+        # the backward pass (no counterpart in the reference): FLOPs counted
+        # as 2.5x the forward's, the usual convention (5 GEMMs against 2)
+        from flash_attention._C import forward_with_lse
+        from flash_attention.backward import flash_attn_backward
+
+        for causal_b in sorted({cfg["causal"], True}):
+            o_b, lse_b = forward_with_lse(q, k, v, causal_b)
+            do_b = torch.randn_like(q)
+            ms_b, _ = device_timed(lambda q_, k_, v_: flash_attn_backward(do_b, q_, k_, v_, o_b, lse_b, causal_b),
+                                   (q, k, v), max(3, a.steps // 4), a.warmup, dist_)
+            fl_b = 2.5 * flops(b, s, h, d, causal_b)
+            variants[f"{a.config}_backward{'_causal' if causal_b else ''}"] = {
+                "value": round(fl_b * a.gpus / (ms_b * 1e-3) / 1e12, 2),
+                "unit": "TFLOPS (2.5x forward FLOPs)",
+                "ms_per_step": round(ms_b, 4),
+            }
+            del o_b, lse_b, do_b
+
     # e2e through the public call with host buffers.
     qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
     oh = torch.empty_like(qh).pin_memory()
