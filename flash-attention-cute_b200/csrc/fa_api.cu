@@ -258,12 +258,18 @@ int check_bwd_params(const FaBwdParams* p) {
   if (p->heads % p->heads_k != 0) return FA_ERR_INVALID_ARG;
   if (!std::isfinite(p->softmax_scale)) return FA_ERR_INVALID_ARG;
   if (p->batch == 0 || (p->seqlen_q == 0 && p->seqlen_k == 0)) return FA_OK;
-  const void* ptrs[] = {p->q, p->k, p->v, p->o, p->dout, p->dq, p->dk, p->dv};
-  for (const void* q : ptrs) {
-    if (q == nullptr) return FA_ERR_INVALID_ARG;
+  // Tensors with no rows (seqlen 0) may have null storage.
+  const void* qside[] = {p->q, p->o, p->dout, p->dq};
+  const void* kside[] = {p->k, p->v, p->dk, p->dv};
+  for (const void* q : qside) {
+    if (p->seqlen_q > 0 && q == nullptr) return FA_ERR_INVALID_ARG;
     if (!aligned16(q)) return FA_ERR_ALIGNMENT;
   }
-  if (p->lse == nullptr || p->dvec == nullptr) return FA_ERR_INVALID_ARG;
+  for (const void* k : kside) {
+    if (p->seqlen_k > 0 && k == nullptr) return FA_ERR_INVALID_ARG;
+    if (!aligned16(k)) return FA_ERR_ALIGNMENT;
+  }
+  if (p->seqlen_q > 0 && (p->lse == nullptr || p->dvec == nullptr)) return FA_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(p->lse) & 3u) || (reinterpret_cast<uintptr_t>(p->dvec) & 3u)) {
     return FA_ERR_ALIGNMENT;
   }

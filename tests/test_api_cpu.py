@@ -45,3 +45,12 @@ def test_host_streaming_rejects_unpinned_tensors():
     with pytest.raises(RuntimeError, match="contiguous"):
         y = torch.zeros(1, 8, 2, 128, dtype=torch.float16)[..., ::2]
         flash_attn_func_host(y, y, y)
+
+
+def test_backward_binding_matches_library_struct():
+    import ctypes
+
+    from flash_attention import _C
+    from flash_attention.backward import FaBwdParams
+
+    assert _C.lib.fa_sm100_bwd_params_size() == ctypes.sizeof(FaBwdParams)

@@ -86,3 +86,23 @@ def test_autograd_function():
     o.backward(do.cuda())
     ref = math_attention_backward(q, k, v, do, True)
     _check((qd.grad, kd.grad, vd.grad), _lowp_grads(q, k, v, do, True, 0), ref)
+
+
+def test_backward_empty_keys_and_strided_dout():
+    from flash_attention._C import forward_with_lse
+    from flash_attention.backward import flash_attn_backward
+
+    q = torch.randn(1, 64, 2, 64, device="cuda", dtype=torch.float16)
+    k = torch.empty(1, 0, 2, 64, device="cuda", dtype=torch.float16)
+    o = torch.zeros_like(q)
+    lse = torch.full((1, 2, 64), float("-inf"), device="cuda")
+    dq, dk, dv = flash_attn_backward(torch.randn_like(q), q, k, k, o, lse, False)
+    assert dk.numel() == 0 and dv.numel() == 0 and bool((dq == 0).all())
+    # dO given as a non-contiguous view gives the same gradients as its copy
+    q, k, v = (t.cuda() for t in make_inputs(1, 256, 2, 128, torch.bfloat16, seed=76))
+    o, lse = forward_with_lse(q, k, v, True)
+    do_big = torch.randn(1, 256, 2, 256, device="cuda", dtype=torch.bfloat16)
+    do = do_big[..., ::2]
+    a = flash_attn_backward(do, q, k, v, o, lse, True)
+    b = flash_attn_backward(do.contiguous(), q, k, v, o, lse, True)
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
