@@ -88,8 +88,8 @@ struct BwdTraits {
   static constexpr int kBoxBytes = kBlockM * 128;
   static constexpr int kNumBoxes = D / 64;
   static constexpr int kStages = D == 128 ? 4 : 8;
-  // q_full, kv_full/empty[NS], s_full, ds_full, acc_done, mma_drain
-  static constexpr int kNumBarriers = 1 + 2 * kStages + 4;
+  // q_full, kv_full/empty[NS], s_full, s_free, ds_full[2], ds_free[2], acc_done, mma_drain
+  static constexpr int kNumBarriers = 1 + 2 * kStages + 8;
   static constexpr int kSmemBytes = 1024 + (2 + kStages) * kTileBytes + kNumBarriers * 8 + 16;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -128,13 +128,19 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
   uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + NS;
   uint64_t* s_full = kv_empty + NS;  // S and dP of the block are in TMEM
-  uint64_t* ds_full = s_full + 1;    // dS of the block is in TMEM
-  uint64_t* acc_done = ds_full + 1;  // every dQ MMA has completed
+  uint64_t* s_free = s_full + 1;     // the elementwise warps hold S and dP in registers
+  uint64_t* ds_full = s_free + 1;    // [2] dS of the buffer's block is in TMEM
+  uint64_t* ds_free = ds_full + 2;   // [2] dQ += dS K of the buffer's last block is done
+  uint64_t* acc_done = ds_free + 2;  // every dQ MMA has completed
   uint64_t* mma_drain = acc_done + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
   volatile int* vabort = abort_flag;
-  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256;
+  // S, dP, the dQ accumulator and two dS buffers (16-bit pairs) all have
+  // their own columns, so the next block's S and dP are computed while the
+  // elementwise warps still work on this block.
+  constexpr uint32_t kColS = 0, kColDP = 128, kColDQ = 256, kColDS = 256 + D;
+  static_assert(kColDS + 128 <= 512, "TMEM budget");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -170,7 +176,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
       mbar_init(smem_u32(&kv_empty[i]), 1);
     }
     mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(ds_full), 2 * kBlockM);
+    mbar_init(smem_u32(s_free), 2 * kBlockM);
+    mbar_init(smem_u32(&ds_full[0]), 2 * kBlockM);
+    mbar_init(smem_u32(&ds_full[1]), 2 * kBlockM);
+    mbar_init(smem_u32(&ds_free[0]), 1);
+    mbar_init(smem_u32(&ds_free[1]), 1);
     mbar_init(smem_u32(acc_done), 1);
     mbar_init(smem_u32(mma_drain), 1);
     const int poisoned = p.error_flag != nullptr ? *reinterpret_cast<volatile int32_t*>(p.error_flag) : 0;
@@ -278,14 +288,14 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
         }
         __syncwarp();
       };
-      auto issue_dq = [&](int kslot, bool acc) {
+      auto issue_dq = [&](int kslot, uint32_t acol, bool acc) {
         // dQ += dS K: dS from TMEM (8 columns of pairs per 16 keys), K_j as an
         // MN-major operand (the forward's O += P V form).
         if (leader) {
           const uint64_t b0 = desc_mn0 + kslot * kSlotStep;
 #pragma unroll
           for (int kk = 0; kk < kBlockN / 16; ++kk) {
-            umma_ts(tmem + kColDQ, tmem + kColS + kk * 8, b0 + kk * (2048 >> 4), kIdescDQ,
+            umma_ts(tmem + kColDQ, tmem + acol + kk * 8, b0 + kk * (2048 >> 4), kIdescDQ,
                     (acc || kk > 0) ? 1u : 0u);
           }
         }
@@ -297,25 +307,42 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
       };
       bool ok = wait_all(q_full, 0);
       int it = 0;
-      for (int j = 0; j < n_blocks && ok; ++j) {
-        const int kslot = it % NS;
-        ok = wait_all(&kv_full[kslot], static_cast<uint32_t>(it / NS) & 1u);
+      int kslot_cur = 0, kslot_next = 0;
+      // K_j and V_j in fill order; S and dP of block 0 first.
+      auto issue_sdp = [&](int& kslot) {
+        kslot = it % NS;
+        bool r = wait_all(&kv_full[kslot], static_cast<uint32_t>(it / NS) & 1u);
         ++it;
         const int vslot = it % NS;
-        ok = ok && wait_all(&kv_full[vslot], static_cast<uint32_t>(it / NS) & 1u);
+        r = r && wait_all(&kv_full[vslot], static_cast<uint32_t>(it / NS) & 1u);
         ++it;
-        if (!ok) break;
+        if (!r) return false;
         tc_fence_after();
         issue_ss(kColS, desc_q, kslot);    // S = Q K_j^T
         issue_ss(kColDP, desc_do, vslot);  // dP = dO V_j^T
         commit(s_full);
         commit(&kv_empty[vslot]);
-        issued = true;
-        ok = wait_all(ds_full, static_cast<uint32_t>(j) & 1u);
+        return true;
+      };
+      if (ok && n_blocks > 0) {
+        ok = issue_sdp(kslot_cur);
+        issued = ok;
+      }
+      for (int j = 0; j < n_blocks && ok; ++j) {
+        const uint32_t ph = static_cast<uint32_t>(j) & 1u;
+        if (j + 1 < n_blocks) {
+          // S/dP of block j+1 once the elementwise warps hold block j's
+          ok = wait_all(s_free, ph) && issue_sdp(kslot_next);
+          if (!ok) break;
+        }
+        // per-buffer barriers: block j's is at most one phase ahead of this wait
+        ok = wait_all(&ds_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u);
         if (!ok) break;
         tc_fence_after();
-        issue_dq(kslot, j > 0);
-        commit(&kv_empty[kslot]);
+        issue_dq(kslot_cur, kColDS + (j & 1) * 64, j > 0);  // dQ += dS_j K_j
+        commit(&ds_free[j & 1]);
+        commit(&kv_empty[kslot_cur]);
+        kslot_cur = kslot_next;
       }
       if (issued) {
         commit(acc_done);
@@ -363,6 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
 #pragma unroll
         for (int i = 0; i < 64; ++i) dpv[i] = __uint_as_float(raw[i]);
       }
+      // S and dP are in registers: the MMA warp may compute the next block's.
+      tc_fence_before();
+      mbar_arrive(smem_u32(s_free));
       const int col0 = j * kBlockN + key_half * 64;
       int64_t valid = row_live ? static_cast<int64_t>(p.seqlen_k) - col0 : 0;
       if constexpr (kCausal) {
@@ -371,18 +401,25 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
       }
       uint32_t pk[32];
       ds_pack<kBf16>(sv, dpv, c, neg, dd, valid, pk);
-      // dS over the first 64 S columns: lanes 0-15 columns [0,32), lanes
-      // 16-31 the same columns of the second key half (32 further).
+      // dS buffer j&1 is free once dQ += dS_{j-2} K_{j-2} has completed.
+      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&ds_free[j & 1]),
+                                                      static_cast<uint32_t>((j - 2) >> 1) & 1u, vabort, tmo))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // lanes 0-15 columns [0,32) of the buffer, lanes 16-31 the same columns
+      // of the second key half (32 further).
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t chunk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) chunk[i] = pk[16 * h + i];
-        tmem_st_16x32bx2_x16<32>(tmem + lane_addr + kColS + h * 16, chunk);
+        tmem_st_16x32bx2_x16<32>(tmem + lane_addr + kColDS + (j & 1) * 64 + h * 16, chunk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(smem_u32(ds_full));
+      mbar_arrive(smem_u32(&ds_full[j & 1]));
     }
     // ---- epilogue: dQ = scale * (dS K), in the input type.
     bool have = ok && n_blocks > 0;
