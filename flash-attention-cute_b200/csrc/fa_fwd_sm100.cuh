@@ -88,7 +88,7 @@ struct FwdTraits {
 // Pairs (out of every 16) whose exp2 runs on the FMA pipe (exp2_poly2)
 // instead of MUFU: at head_dim 128 the MUFU unit alone needs as many cycles
 // as the tensor core per block, so part of the work is moved.
-constexpr int kEmuPer16 = 5;
+constexpr int kEmuPer16 = 3;
 __host__ __device__ constexpr bool emulated_pair(int i) { return (i * kEmuPer16) % 16 < kEmuPer16; }
 
 // P = exp2(s * c + neg) for one N-key slice of a row: packs P to 16-bit
