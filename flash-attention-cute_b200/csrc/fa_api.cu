@@ -160,6 +160,18 @@ uint64_t timeout_ns() {
   return o != 0 ? o : default_timeout_ns();
 }
 
+// The TMA descriptors are encoded through the driver API, which needs the
+// device's context current in the calling thread.  A thread that has made no
+// runtime call yet (an autograd worker, a fresh host thread) may not have it:
+// bind it once per thread and device.
+int bind_context(int dev) {
+  thread_local int bound = -1;
+  if (bound == dev) return FA_OK;
+  if (cudaSetDevice(dev) != cudaSuccess) return FA_ERR_CUDA;
+  bound = dev;
+  return FA_OK;
+}
+
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 bool stride_ok(int64_t s) { return s >= 0 && (s % 8) == 0; }  // 16 bytes of 16-bit elements
 
@@ -321,7 +333,7 @@ int fa_sm100_fwd(const FaParams* p, void* stream_ptr) {
   if (p->batch == 0 || p->seqlen_q == 0) return FA_OK;
 
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  if (cudaGetDevice(&dev) != cudaSuccess || bind_context(dev) != FA_OK) return FA_ERR_CUDA;
   DeviceState* ds = nullptr;
   rc = device_state(dev, &ds);
   if (rc != FA_OK) return rc;
@@ -447,7 +459,7 @@ int fa_sm100_bwd(const FaBwdParams* p, void* stream_ptr) {
   if (rc != FA_OK) return rc;
   if (p->batch == 0 || (p->seqlen_q == 0 && p->seqlen_k == 0)) return FA_OK;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  if (cudaGetDevice(&dev) != cudaSuccess || bind_context(dev) != FA_OK) return FA_ERR_CUDA;
   DeviceState* ds = nullptr;
   rc = device_state(dev, &ds);
   if (rc != FA_OK) return rc;

@@ -261,3 +261,36 @@ def test_lse_merge_recovers_full_attention():
     o_ref, lse_ref = math_attention(q, k, v, True, q_pos_offset=300)
     assert (out.float().cpu() - o_ref[0]).abs().max() <= O_TOL[torch.bfloat16]
     assert _lse_err(lse, lse_ref[0]) <= LSE_TOL
+
+
+def test_calls_from_fresh_host_threads():
+    """Forward and backward called from a host thread that has made no CUDA
+    call before (as autograd's worker threads do) bind the device themselves."""
+    import threading
+
+    from flash_attention import flash_attn_func
+    from flash_attention._C import forward_with_lse
+    from flash_attention.backward import flash_attn_backward
+
+    q, k, v = (t.cuda() for t in make_inputs(1, 256, 2, 128, torch.bfloat16, seed=81))
+    do = torch.randn_like(q)
+    want_o = flash_attn_func(q, k, v, True)
+    o, lse = forward_with_lse(q, k, v, True)
+    want_g = flash_attn_backward(do, q, k, v, o, lse, True)
+    torch.cuda.synchronize()
+    got = {}
+
+    def work():
+        try:
+            got["o"] = flash_attn_func(q, k, v, True)
+            got["g"] = flash_attn_backward(do, q, k, v, o, lse, True)
+            torch.cuda.synchronize()
+        except Exception as e:  # noqa: BLE001 - reported by the main thread
+            got["err"] = e
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    assert "err" not in got, got.get("err")
+    assert torch.equal(got["o"], want_o)
+    assert all(torch.equal(a, b) for a, b in zip(got["g"], want_g))
