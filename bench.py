@@ -212,28 +212,67 @@ def make_shard(cfg, rank, device, seed=0):
     return [torch.randn((b, s, h, d), generator=g, device=device, dtype=torch.float32).to(dtype) for _ in range(3)]
 
 
+def fits_in_l2(args) -> bool:
+    """True when the step's input tensors together fit in this GPU's L2."""
+    size = sum(t.numel() * t.element_size() for t in args if isinstance(t, torch.Tensor))
+    return size <= torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+
+
+def l2_note(args) -> str:
+    size = sum(t.numel() * t.element_size() for t in args if isinstance(t, torch.Tensor))
+    if fits_in_l2(args):
+        return (f"inputs ({size / 2**20:.0f} MiB) fit in L2: a buffer of twice the L2 size is written before "
+                "every step, outside the event pair that times the step")
+    return f"inputs larger than L2 (q/k/v = {size / 2**30:.2f} GiB per step), no flush"
+
+
 def device_timed(fn, args, steps, warmup, dist_, clocks=None):
-    """Returns (ms per step over the whole timed region (max over ranks),
-    mean per-launch device ms on this rank)."""
+    """Returns (ms per step (max over ranks), mean per-launch device ms on
+    this rank).
+
+    Inputs larger than L2: the K steps run back to back between one pair of
+    events, with nothing else recorded inside (a per-step event costs host time
+    that shows at small sizes); the per-launch duration comes from a second,
+    separately bracketed pass with an event pair around each launch.
+    Inputs that fit in L2: before each step a buffer of twice the L2 size is
+    written (evicting the previous step's lines), outside an event pair around
+    the step alone; ms per step is the mean of those pairs."""
     for _ in range(warmup):
         fn(*args)
     torch.cuda.synchronize()
     dist_.barrier()
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx = clocks if clocks is not None else _Null()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if fits_in_l2(args):
+        flush = torch.empty(2 * torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size,
+                            dtype=torch.uint8, device="cuda")
+        with ctx:
+            for e0, e1 in evs:
+                flush.fill_(1)
+                e0.record()
+                fn(*args)
+                e1.record()
+            torch.cuda.synchronize()
+        dist_.barrier()
+        per_launch = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+        return dist_.max(per_launch), per_launch
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ctx:
         start.record()
-        for e0, e1 in evs:
-            e0.record()
+        for _ in range(steps):
             fn(*args)
-            e1.record()
         end.record()
         torch.cuda.synchronize()
     dist_.barrier()
     torch.cuda.synchronize()
     total = start.elapsed_time(end)
+    for e0, e1 in evs:
+        e0.record()
+        fn(*args)
+        e1.record()
+    torch.cuda.synchronize()
+    dist_.barrier()
     per_launch = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
     return dist_.max(total) / steps, per_launch
 
@@ -246,8 +285,20 @@ class _Null:
         return False
 
 
-def e2e_timed(fn, host_in, dev_in, host_out_fn, steps, dist_):
-    """Per step: H2D of q/k/v from pinned memory, the call, D2H of outputs."""
+def _e2e_step_count(call, min_steps, dist_, target_s=0.25):
+    """Steps for a timed region of about target_s, at least min_steps, the
+    same on every rank: one more warm call, timed on the host, sets it."""
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    call()
+    torch.cuda.synchronize()
+    el = dist_.max(time.perf_counter() - t0)
+    return max(min_steps, min(1000, int(target_s / max(el, 1e-6))))
+
+
+def e2e_timed(fn, host_in, dev_in, host_out_fn, min_steps, dist_):
+    """Per step: H2D of q/k/v from pinned memory, the call, D2H of outputs.
+    Returns (ms per step, steps timed)."""
     qh, kh, vh = host_in
     qd, kd, vd = dev_in
 
@@ -259,6 +310,7 @@ def e2e_timed(fn, host_in, dev_in, host_out_fn, steps, dist_):
         host_out_fn(out)
 
     step()
+    steps = _e2e_step_count(step, min_steps, dist_)
     torch.cuda.synchronize()
     dist_.barrier()
     torch.cuda.synchronize()
@@ -269,12 +321,14 @@ def e2e_timed(fn, host_in, dev_in, host_out_fn, steps, dist_):
     end.record()
     torch.cuda.synchronize()
     dist_.barrier()
-    return dist_.max(start.elapsed_time(end)) / steps
+    return dist_.max(start.elapsed_time(end)) / steps, steps
 
 
-def e2e_streamed(call, steps, dist_):
-    """Per step: one blocking host-to-host call (it copies q/k/v in and O/LSE out)."""
+def e2e_streamed(call, min_steps, dist_):
+    """Per step: one blocking host-to-host call (it copies q/k/v in and O/LSE
+    out).  Returns (ms per step, steps timed)."""
     call()
+    steps = _e2e_step_count(call, min_steps, dist_)
     torch.cuda.synchronize()
     dist_.barrier()
     torch.cuda.synchronize()
@@ -285,7 +339,7 @@ def e2e_streamed(call, steps, dist_):
     end.record()
     torch.cuda.synchronize()
     dist_.barrier()
-    return dist_.max(start.elapsed_time(end)) / steps
+    return dist_.max(start.elapsed_time(end)) / steps, steps
 
 
 def cpu_baseline(cfg, budget_s=12.0):
@@ -400,7 +454,7 @@ def run_context_parallel(a, dist_):
                 )
                 if a.gpus > 1
                 else "single GPU",
-                "l2": "inputs larger than L2 (q/k/v = 1 GiB each)",
+                "l2": l2_note((q, k, v)) + " on each rank",
                 "flops_per_step_total": fl,
             },
             "impl": a.impl,
@@ -426,7 +480,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="C4", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=3, help="minimum e2e steps (more for short steps)")
     ap.add_argument("--no-variants", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true", help="skip NVML clock sampling")
@@ -484,6 +538,7 @@ def main():
     fn, desc = build_fn(a.impl, cfg, cfg["causal"])
     clocks = ClockSampler(dist_.local) if not a.no_clocks else None
     ms, launch_ms = device_timed(fn, (q, k, v), a.steps, a.warmup, dist_, clocks)
+    l2_of_step = l2_note((q, k, v))
     value = fl * a.gpus / (ms * 1e-3) / 1e12
     achieved = fl / (launch_ms * 1e-3) / 1e12
 
@@ -538,12 +593,12 @@ def main():
         from flash_attention import flash_attn_func_host
 
         del qd, kd, vd
-        ms_e2e = e2e_streamed(lambda: flash_attn_func_host(qh, kh, vh, cfg["causal"], out=oh, lse_out=lseh),
+        ms_e2e, e2e_steps = e2e_streamed(lambda: flash_attn_func_host(qh, kh, vh, cfg["causal"], out=oh, lse_out=lseh),
                               a.e2e_steps, dist_)
         e2e_how = ("pinned host q/k/v -> flash_attn_func_host -> pinned host O + LSE: batch chunks stream through "
                    "the GPU, H2D / kernel / D2H of different chunks overlapped on three streams")
     else:
-        ms_e2e = e2e_timed(fn, (qh, kh, vh), (qd, kd, vd), host_out, a.e2e_steps, dist_)
+        ms_e2e, e2e_steps = e2e_timed(fn, (qh, kh, vh), (qd, kd, vd), host_out, a.e2e_steps, dist_)
         e2e_how = "pinned host q/k/v -> device, the public call, O (+LSE) -> pinned host; one stream"
     h2d = 3 * qh.numel() * qh.element_size()
     d2h = oh.numel() * oh.element_size() + (lseh.numel() * 4 if a.impl == "ours" else 0)
@@ -580,7 +635,7 @@ def main():
                 "head_dim": d,
                 "causal": cfg["causal"],
                 "parallelism": f"batch x head sharding over {a.gpus} GPU(s), no collective",
-                "l2": "inputs larger than L2 (q/k/v/o = %.1f GiB per step), no flush" % (4 * qh.numel() * 2 / 2**30),
+                "l2": l2_of_step,
                 "flops_per_step_per_gpu": fl,
             },
             "impl": a.impl,
@@ -603,7 +658,7 @@ def main():
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(ms_e2e, 3),
-                "steps": a.e2e_steps,
+                "steps": e2e_steps,
                 "how": e2e_how,
             },
             "gpu_launches": a.steps if a.impl == "ours" else 0,

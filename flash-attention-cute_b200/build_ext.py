@@ -40,6 +40,18 @@ NVCC_FLAGS = ARCH_FLAGS + [
 ]
 
 
+# The pybind11 module (flash_attention/_fa_torch*.so): the C++ per-call path
+# of forward(), linked against libfa_sm100.so through $ORIGIN.
+BINDING_SOURCE = os.path.join(CSRC, "fa_torch_binding.cpp")
+BINDING_NAME = "_fa_torch"
+
+
+def binding_path() -> str:
+    import sysconfig
+
+    return os.path.join(PKG, BINDING_NAME + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
 def _nvcc() -> str:
     cand = os.environ.get("NVCC") or shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     if not os.path.exists(cand):
@@ -76,6 +88,40 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     return LIB_PATH
 
 
+def build_binding(force: bool = False, verbose: bool = False) -> str:
+    """Compile the pybind11 module with the host C++ compiler against torch's
+    headers; needs libfa_sm100.so built first (it links against it)."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    out = binding_path()
+    deps = [BINDING_SOURCE, os.path.join(INCLUDE, "fa_sm100.h"), os.path.abspath(__file__), LIB_PATH]
+    if not force and os.path.exists(out) and all(os.path.getmtime(f) <= os.path.getmtime(out) for f in deps):
+        return out
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "c++"
+    incs = [*cpp_extension.include_paths("cuda"), sysconfig.get_paths()["include"], INCLUDE]
+    libdirs = cpp_extension.library_paths("cuda")[:1]  # torch's own lib folder
+    tmp = out + ".tmp"
+    cmd = [
+        cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+        f"-DTORCH_EXTENSION_NAME={BINDING_NAME}", "-DTORCH_API_INCLUDE_EXTENSION_H",
+        f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+        *[f"-I{i}" for i in incs], BINDING_SOURCE, "-o", tmp,
+        *[f"-L{d}" for d in libdirs], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+        f"-L{PKG}", "-lfa_sm100", "-Wl,-rpath,$ORIGIN",
+    ]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"binding build failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, out)
+    return out
+
+
 if __name__ == "__main__":
     path = build(force="--force" in sys.argv, verbose=True)
     print(path)
+    print(build_binding(force="--force" in sys.argv, verbose=True))

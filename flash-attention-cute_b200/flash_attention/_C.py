@@ -6,16 +6,18 @@ behaviour: the same input checks with the same messages raised as
 ``RuntimeError`` (csrc/flash_api.cpp:14-29), output allocated with
 ``torch.empty_like(q)`` (flash_api.cpp:31), softmax scale ``1/sqrt(d)``
 (flash_api.cpp:59-60), launched on the current stream of q's device
-(flash_api.cpp:64; a device guard is added).  The native call goes through
-the C ABI declared in ``include/fa_sm100.h`` via ctypes; there is no CPU
-path: if the library is missing, importing this module fails.
+(flash_api.cpp:64; a device guard is added).  ``forward`` and
+``forward_with_lse`` run in the pybind11 module ``_fa_torch``
+(csrc/fa_torch_binding.cpp), which calls the C ABI declared in
+``include/fa_sm100.h``; the other entry points bind that C ABI through ctypes.
+There is no CPU path: if either native module is missing, importing this
+module fails.
 """
 from __future__ import annotations
 
 import ctypes
 import math
 import os
-import struct
 
 import torch
 
@@ -109,22 +111,19 @@ def _load() -> ctypes.CDLL:
 
 lib = _load()
 
-# Fast launch path: FaParams packed with one struct.pack call (layout checked
-# against the ctypes mirror below) and passed as a byte buffer.  For small
-# problems the per-call host cost is comparable to the kernel itself.
-_PACKED = struct.Struct("=5Q6i14qf2i4x2qQi4x")
-_fwd_packed = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_char_p, ctypes.c_void_p)(("fa_sm100_fwd", lib))
-_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
-
-
-def _check_packed_layout() -> None:
-    vals = (1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, *range(12, 26), 0.5, 1, 1, 26, 27, 28, 1)
-    mirror = FaParams(*vals)
-    if _PACKED.size != ctypes.sizeof(FaParams) or _PACKED.pack(*vals) != bytes(mirror):
-        raise ImportError("packed FaParams layout does not match the ctypes mirror")
-
-
-_check_packed_layout()
+# The per-call path of forward(): a pybind11 module (csrc/fa_torch_binding.cpp)
+# that runs the checks, allocates O / LSE and calls fa_sm100_fwd in C++, as the
+# reference's own compiled _C.forward does.  It links against the library
+# loaded above, so both share one copy of its state.
+try:
+    from flash_attention import _fa_torch as _ext
+except ImportError as e:
+    raise ImportError(
+        f"the flash_attention._fa_torch module is missing or broken ({e}): build it with "
+        "`python flash-attention-cute_b200/build_ext.py` (there is no fallback implementation)"
+    ) from e
+if _ext.params_size() != ctypes.sizeof(FaParams):
+    raise ImportError("flash_attention._fa_torch was built against another FaParams layout")
 
 
 def status_string(rc: int) -> str:
@@ -196,17 +195,6 @@ def fill_params(
     )
 
 
-def launch(p: FaParams, device: torch.device) -> None:
-    """Enqueue the kernel for filled params on the current stream of `device`."""
-    if device.index is None or device.index == torch.cuda.current_device():
-        stream = torch.cuda.current_stream().cuda_stream
-        _check(lib.fa_sm100_fwd(ctypes.byref(p), stream), "fa_sm100_fwd")
-        return
-    with torch.cuda.device(device):
-        stream = torch.cuda.current_stream(device).cuda_stream
-        _check(lib.fa_sm100_fwd(ctypes.byref(p), stream), "fa_sm100_fwd")
-
-
 def forward_with_lse(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -220,41 +208,16 @@ def forward_with_lse(
     out: torch.Tensor | None = None,
     lse_out: torch.Tensor | None = None,
 ):
-    _validate(q, k, v)
-    if out is not None and (out.shape != q.shape or out.dtype not in (q.dtype, torch.float32)
-                            or out.device != q.device or out.stride(-1) != 1):
-        raise RuntimeError("out must match q's shape and device, with q's dtype or fp32, contiguous in last dim")
-    b, sq, h, d = q.shape
-    o = torch.empty_like(q) if out is None else out
-    lse = None
-    if want_lse:
-        lse = q.new_empty((b, h, sq), dtype=torch.float32) if lse_out is None else lse_out
-    qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), o.stride()
-    ls = lse.stride() if lse is not None else (0, 0, 0)
-    packed = _PACKED.pack(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr() if lse is not None else 0,
-        b, sq, k.shape[1], h, k.shape[2], d,
-        qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1], vs[2], os_[0], os_[1], os_[2], ls[0], ls[1],
-        (1.0 / math.sqrt(d)) if softmax_scale is None else float(softmax_scale),
-        1 if causal else 0,
-        1 if q.dtype == torch.bfloat16 else 0,
-        int(q_pos_offset), int(k_pos_offset), 0,
-        1 if o.dtype == torch.float32 else 0,
-    )
-    idx = q.device.index
-    if idx == torch.cuda.current_device():
-        stream = _raw_stream(idx) if _raw_stream is not None else torch.cuda.current_stream().cuda_stream
-        _check(_fwd_packed(packed, stream), "fa_sm100_fwd")
-    else:
-        with torch.cuda.device(q.device):
-            _check(_fwd_packed(packed, torch.cuda.current_stream(q.device).cuda_stream), "fa_sm100_fwd")
-    return o, lse
+    """O and LSE ((batch, heads, seqlen_q) fp32, natural log; None unless
+    want_lse) of attention over q, k, v.  `out` / `lse_out` are optional
+    destinations; `out` may be fp32 (partial results for a later LSE merge).
+    Launched on the current stream of q's device."""
+    return _ext.forward_with_lse(q, k, v, causal, softmax_scale, q_pos_offset, k_pos_offset, want_lse, out, lse_out)
 
 
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool) -> torch.Tensor:
     """``flash_attention._C.forward(q, k, v, causal) -> o`` (csrc/flash_api.cpp:9-68)."""
-    o, _ = forward_with_lse(q, k, v, causal, want_lse=False)
-    return o
+    return _ext.forward(q, k, v, causal)
 
 
 def lse_merge(o_parts, lse_parts, o_out: torch.Tensor, lse_out: torch.Tensor | None = None) -> None:

@@ -54,3 +54,27 @@ def test_backward_binding_matches_library_struct():
     from flash_attention.backward import FaBwdParams
 
     assert _C.lib.fa_sm100_bwd_params_size() == ctypes.sizeof(FaBwdParams)
+
+
+def test_pybind_module_exports_and_shares_the_library():
+    """forward() runs in the pybind11 module, which links the same
+    libfa_sm100.so that ctypes loaded (one copy of its state in the process)."""
+    import inspect
+
+    from flash_attention import _C, _fa_torch
+
+    assert "forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool)" in _fa_torch.forward.__doc__
+    assert callable(_fa_torch.forward_with_lse)
+    assert _fa_torch.params_size() == _C.lib.fa_sm100_params_size()
+    assert list(inspect.signature(_C.forward).parameters) == ["q", "k", "v", "causal"]
+    with open("/proc/self/maps") as f:
+        paths = {line.split()[-1] for line in f if line.rstrip().endswith("libfa_sm100.so")}
+    assert len(paths) == 1, paths
+
+
+def test_pybind_module_error_messages_on_cpu():
+    from flash_attention._fa_torch import forward
+
+    x = torch.zeros(1, 4, 2, 64)
+    with pytest.raises(RuntimeError, match="q must be on CUDA"):
+        forward(x, x, x, False)
