@@ -13,12 +13,14 @@
 //   * warp 9 is the MMA issuer: tcgen05.mma S_t = Q_t K_j^T (both operands in
 //     shared memory, accumulator in TMEM) and O_t += P_t V_j (P read straight
 //     from TMEM, V in shared memory as an MN-major operand -- no transpose);
-//   * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: thread r
-//     owns query row r, which is TMEM lane r.  They read S with tcgen05.ld,
-//     mask (tail / causal), update the running max, rescale O in TMEM only
-//     when the max grew by more than 2^8 (the final division uses the same
-//     stale max, so the result is exact), write P over S as 16-bit pairs and
-//     finally normalise O and store O and LSE.
+//   * warps 0-7 are the softmax warps: all eight work on one query tile at a
+//     time (tile 0, then tile 1, every key block).  Warp w owns 16 TMEM lanes
+//     (rows) of its quarter w & 3; with the 16x32bx2 access shape each thread
+//     holds one row and one 64-key half of the block.  They read S with
+//     tcgen05.ld, mask (tail / causal), update the running max, rescale O in
+//     TMEM only when the max grew by more than 2^8 (the final division uses
+//     the same stale max, so the result is exact), write P over S as 16-bit
+//     pairs and finally normalise O and store O and LSE.
 //
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // Every mbarrier wait is bounded; on expiry the CTA records FA_ERR_TIMEOUT,
