@@ -465,8 +465,8 @@ struct BwdKVTraits {
   // stage = Q_i, dO_i tiles + 128 floats of -LSE*log2(e) + 128 floats of D
   static constexpr int kStageBytes = 2 * kTileBytes + 1024;
   static constexpr int kStages = D == 128 ? 2 : 4;
-  // kv_full, st_full/empty[NS], s_full, p_full, acc_done, mma_drain
-  static constexpr int kNumBarriers = 1 + 2 * kStages + 4;
+  // kv_full, st_full/empty[NS], s_full[2], p_full[2], acc_done, mma_drain
+  static constexpr int kNumBarriers = 1 + 2 * kStages + 6;
   static constexpr int kSmemBytes = 1024 + 2 * kTileBytes + kStages * kStageBytes + kNumBarriers * 8 + 16;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D;
@@ -487,9 +487,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
   uint64_t* kv_full = bars;
   uint64_t* st_full = kv_full + 1;
   uint64_t* st_empty = st_full + NS;
-  uint64_t* s_full = st_empty + NS;  // S^T and dP^T of the step are in TMEM
-  uint64_t* p_full = s_full + 1;     // P^T and dS^T are in TMEM
-  uint64_t* acc_done = p_full + 1;
+  // Each step's 128 query columns are processed as two halves of 64, so the
+  // elementwise work on one half overlaps the other half's MMAs.
+  uint64_t* s_full = st_empty + NS;  // [2] S^T and dP^T of the half are in TMEM
+  uint64_t* p_full = s_full + 2;     // [2] P^T and dS^T of the half are in TMEM
+  uint64_t* acc_done = p_full + 2;
   uint64_t* mma_drain = acc_done + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
@@ -524,8 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
       mbar_init(smem_u32(&st_full[i]), 1);
       mbar_init(smem_u32(&st_empty[i]), 1);
     }
-    mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(p_full), 2 * kBlockM);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(smem_u32(&s_full[h]), 1);
+      mbar_init(smem_u32(&p_full[h]), 2 * kBlockM);
+    }
     mbar_init(smem_u32(acc_done), 1);
     mbar_init(smem_u32(mma_drain), 1);
     const int poisoned = p.error_flag != nullptr ? *reinterpret_cast<volatile int32_t*>(p.error_flag) : 0;
@@ -589,27 +593,32 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
         const int head = kv_head * p.heads_per_kv + g;
         const int slot = it % NS;
         const uint32_t fill = static_cast<uint32_t>(it / NS);
+        // -LSE*log2(e) and D of the block's 128 query rows (bounded loads;
+        // rows past the end, or that saw no key, get -inf so P = 0), read
+        // before waiting for the slot so their latency overlaps the wait.
+        float v_nl[4], v_d[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = qi * kBlockM + lane * 4 + e;
+          v_nl[e] = -INFINITY;
+          v_d[e] = 0.f;
+          if (row < p.seqlen_q) {
+            const float l = p.lse[static_cast<int64_t>(batch) * p.lse_batch_stride +
+                                  static_cast<int64_t>(head) * p.lse_head_stride + row];
+            v_nl[e] = l == -INFINITY ? -INFINITY : -l * 1.4426950408889634f;
+            v_d[e] = p.dvec[(static_cast<int64_t>(batch) * p.heads + head) * p.seqlen_q + row];
+          }
+        }
         if (!wait_all(&st_empty[slot], (fill & 1u) ^ 1u)) {
           ok = false;
           break;
         }
-        // -LSE*log2(e) and D of the block's 128 query rows (bounded loads;
-        // rows past the end, or that saw no key, get -inf so P = 0).
         float* nl = stage_nl(slot);
         float* ddv = stage_dd(slot);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int rr = lane * 4 + e;
-          const int row = qi * kBlockM + rr;
-          float v_nl = -INFINITY, v_d = 0.f;
-          if (row < p.seqlen_q) {
-            const float l = p.lse[static_cast<int64_t>(batch) * p.lse_batch_stride +
-                                  static_cast<int64_t>(head) * p.lse_head_stride + row];
-            v_nl = l == -INFINITY ? -INFINITY : -l * 1.4426950408889634f;
-            v_d = p.dvec[(static_cast<int64_t>(batch) * p.heads + head) * p.seqlen_q + row];
-          }
-          nl[rr] = v_nl;
-          ddv[rr] = v_d;
+          nl[lane * 4 + e] = v_nl[e];
+          ddv[lane * 4 + e] = v_d[e];
         }
         __syncwarp();
         if (leader) {
@@ -635,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
       }
     } else if (warp == 9 && n_steps > 0) {
       // --------------------------------------------------------------- MMA
-      constexpr uint32_t kIdescS = make_idesc_f16(kBlockN, kBlockM, kBf16, false);
+      // S^T / dP^T of one half: M = 128 keys, N = 64 queries
+      constexpr uint32_t kIdescS = make_idesc_f16(kBlockN, kBlockM / 2, kBf16, false);
       constexpr uint32_t kIdescAcc = make_idesc_f16(kBlockN, D, kBf16, true);
       const uint64_t desc_k = make_sw128_desc(smem_u32(sK), 16, 1024);
       const uint64_t desc_v = make_sw128_desc(smem_u32(sV), 16, 1024);
@@ -643,6 +653,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
       const uint64_t desc_mn0 = make_sw128_desc(smem_u32(sStage), Tr::kBoxBytes, 1024);  // MN-major (N = d)
       constexpr uint64_t kStageStep = Tr::kStageBytes >> 4;
       constexpr uint64_t kDoOff = Tr::kTileBytes >> 4;
+      constexpr uint64_t kHalfRows = (64 * 128) >> 4;    // 64 rows of 128-byte-row boxes, K-major
+      constexpr uint64_t kHalfRowsMN = 4 * (2048 >> 4);  // 64 rows = 4 steps of 16, MN-major
       bool issued = false;
       auto issue_ss = [&](uint32_t dcol, uint64_t desc_a, uint64_t desc_b) {
         if (leader) {
@@ -655,10 +667,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
         __syncwarp();
       };
       auto issue_acc = [&](uint32_t dcol, uint32_t acol, uint64_t desc_b, bool acc) {
-        // D(keys x d) += A(keys x queries, 16-bit pairs in TMEM) B(queries x d)
+        // D(keys x d) += A(keys x 64 queries, 16-bit pairs in TMEM) B(queries x d)
         if (leader) {
 #pragma unroll
-          for (int kk = 0; kk < kBlockM / 16; ++kk) {
+          for (int kk = 0; kk < kBlockM / 32; ++kk) {
             umma_ts(tmem + dcol, tmem + acol + kk * 8, desc_b + kk * (2048 >> 4), kIdescAcc,
                     (acc || kk > 0) ? 1u : 0u);
           }
@@ -669,24 +681,49 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
         if (leader) umma_commit(smem_u32(bar));
         __syncwarp();
       };
-      bool ok = wait_all(kv_full, 0);
+      // S^T_h = K Q_h^T and dP^T_h = V dO_h^T for query half h of stage `slot`
+      auto issue_sdp = [&](int slot, int h) {
+        const uint64_t dq_ = desc_st0 + slot * kStageStep + h * kHalfRows;
+        issue_ss(Tr::kColS + 64 * h, desc_k, dq_);
+        issue_ss(Tr::kColDP + 64 * h, desc_v, dq_ + kDoOff);
+        commit(&s_full[h]);
+      };
+      // dV += P^T_h dO_h and dK += dS^T_h Q_h for query half h of stage `slot`
+      auto issue_dvdk = [&](int slot, int h, bool acc) {
+        const uint64_t mq = desc_mn0 + slot * kStageStep + h * kHalfRowsMN;
+        issue_acc(Tr::kColDV, Tr::kColS + 64 * h, mq + kDoOff, acc);
+        issue_acc(Tr::kColDK, Tr::kColDP + 64 * h, mq, acc);
+      };
+      bool ok = wait_all(kv_full, 0) && wait_all(&st_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+        issued = true;
+      }
+      // Per step and half h: dV/dK of half h, then the next step's S^T/dP^T of
+      // half h into the same columns (the MMAs of one issuing thread execute
+      // in order, so the products read P^T_h / dS^T_h before they are
+      // overwritten), while the elementwise warps work on the other half.
       for (int it = 0; it < n_steps && ok; ++it) {
         const int slot = it % NS;
-        ok = wait_all(&st_full[slot], static_cast<uint32_t>(it / NS) & 1u);
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t dq_ = desc_st0 + slot * kStageStep;  // Q_i, K-major
-        issue_ss(Tr::kColS, desc_k, dq_);                   // S^T = K Q_i^T
-        issue_ss(Tr::kColDP, desc_v, dq_ + kDoOff);         // dP^T = V dO_i^T
-        commit(s_full);
-        issued = true;
-        ok = wait_all(p_full, static_cast<uint32_t>(it) & 1u);
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t mq = desc_mn0 + slot * kStageStep;  // Q_i, MN-major
-        issue_acc(Tr::kColDV, Tr::kColS, mq + kDoOff, it > 0);  // dV += P^T dO_i
-        issue_acc(Tr::kColDK, Tr::kColDP, mq, it > 0);          // dK += dS^T Q_i
-        commit(&st_empty[slot]);
+        const bool more = it + 1 < n_steps;
+        const int nslot = (it + 1) % NS;
+        for (int h = 0; h < 2 && ok; ++h) {
+          ok = wait_all(&p_full[h], static_cast<uint32_t>(it) & 1u);
+          if (!ok) break;
+          tc_fence_after();
+          issue_dvdk(slot, h, it > 0 || h > 0);
+          if (h == 1) commit(&st_empty[slot]);  // every MMA reading stage `slot` is issued
+          if (more) {
+            if (h == 0) {
+              ok = wait_all(&st_full[nslot], static_cast<uint32_t>((it + 1) / NS) & 1u);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_sdp(nslot, h);
+          }
+        }
       }
       if (issued) {
         commit(acc_done);
@@ -700,8 +737,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
     return;
   } else {
     // --------------------------------------------------------- elementwise
-    // Thread: key row r of the block (a TMEM lane) and one half (64) of the
-    // step's 128 query columns.
+    // Thread: key row r of the block (a TMEM lane) and, in each query half of
+    // the step, 32 of its 64 query columns.
     reg_alloc<kRegsSoftmax>();
     const int qh = lane >> 4;
     const int r = 32 * (warp & 3) + 16 * (warp >> 2) + (lane & 15);
@@ -713,60 +750,60 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
     const float c = p.scale_log2;
     bool ok = true;
 #pragma unroll 1
-    for (int it = 0; it < n_steps; ++it) {
+    for (int it = 0; it < n_steps && ok; ++it) {
       const int slot = it % NS;
       const int qi = i_start + it % q_blocks;
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(s_full), static_cast<uint32_t>(it) & 1u, vabort, tmo))) {
-        ok = false;
-        break;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        // query half hh of the step: S^T_hh, dP^T_hh in columns 64 hh + [0, 64);
+        // lanes 0-15 hold its queries [0, 32), lanes 16-31 queries [32, 64)
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[hh]), static_cast<uint32_t>(it) & 1u, vabort, tmo))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t col_s = Tr::kColS + 64 * hh;
+        const uint32_t col_dp = Tr::kColDP + 64 * hh;
+        float sv[32], dpv[32];
+        {
+          uint32_t raw[32];
+          tmem_ld_16x32bx2_x32_sync<32>(tmem + lane_addr + col_s, raw);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(raw[i]);
+          tmem_ld_16x32bx2_x32_sync<32>(tmem + lane_addr + col_dp, raw);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) dpv[i] = __uint_as_float(raw[i]);
+        }
+        // queries [q0, q0 + 32) of this thread; the first `lo` are masked
+        const int64_t q0 = static_cast<int64_t>(qi) * kBlockM + 64 * hh + qh * 32;
+        int64_t lo = 0;
+        if constexpr (kCausal) {
+          const int64_t first_vis = key_pos - p.q_pos_offset - q0;  // first query index that sees the key
+          lo = first_vis < 0 ? 0 : first_vis;
+        }
+        if (!key_ok) lo = 32;
+        const float* nl = stage_nl(slot) + 64 * hh + qh * 32;
+        const float* ddv = stage_dd(slot) + 64 * hh + qh * 32;
+        uint32_t pk_p[16], pk_s[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), make_float2(c, c),
+                                      make_float2(nl[2 * i], nl[2 * i + 1]));
+          float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          if (2 * i < lo) pe.x = 0.f;
+          if (2 * i + 1 < lo) pe.y = 0.f;
+          const float2 g = __fmul2_rn(pe, make_float2(dpv[2 * i] - ddv[2 * i], dpv[2 * i + 1] - ddv[2 * i + 1]));
+          pk_p[i] = pack2<kBf16>(pe.x, pe.y);
+          pk_s[i] = pack2<kBf16>(g.x, g.y);
+        }
+        // P^T_hh over the first 32 columns of S^T_hh, dS^T_hh over those of dP^T_hh
+        // (query q of the half in column q / 2)
+        tmem_st_16x32bx2_x16<16>(tmem + lane_addr + col_s, pk_p);
+        tmem_st_16x32bx2_x16<16>(tmem + lane_addr + col_dp, pk_s);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&p_full[hh]));
       }
-      tc_fence_after();
-      float sv[64], dpv[64];
-      {
-        uint32_t raw[64];
-        tmem_ld_16x32bx2_x64_sync<64>(tmem + lane_addr + Tr::kColS, raw);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
-        tmem_ld_16x32bx2_x64_sync<64>(tmem + lane_addr + Tr::kColDP, raw);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) dpv[i] = __uint_as_float(raw[i]);
-      }
-      // queries [q0, q0 + 64) of this thread; the first `lo` are masked
-      const int64_t q0 = static_cast<int64_t>(qi) * kBlockM + qh * 64;
-      int64_t lo = 0;
-      if constexpr (kCausal) {
-        const int64_t first_vis = key_pos - p.q_pos_offset - q0;  // first query index that sees the key
-        lo = first_vis < 0 ? 0 : first_vis;
-      }
-      if (!key_ok) lo = 64;
-      const float* nl = stage_nl(slot) + qh * 64;
-      const float* ddv = stage_dd(slot) + qh * 64;
-      uint32_t pk_p[32], pk_s[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), make_float2(c, c),
-                                    make_float2(nl[2 * i], nl[2 * i + 1]));
-        float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-        if (2 * i < lo) pe.x = 0.f;
-        if (2 * i + 1 < lo) pe.y = 0.f;
-        const float2 g = __fmul2_rn(pe, make_float2(dpv[2 * i] - ddv[2 * i], dpv[2 * i + 1] - ddv[2 * i + 1]));
-        pk_p[i] = pack2<kBf16>(pe.x, pe.y);
-        pk_s[i] = pack2<kBf16>(g.x, g.y);
-      }
-      // P^T over the first 64 S^T columns, dS^T over the first 64 dP^T columns
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t chunk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) chunk[i] = pk_p[16 * h + i];
-        tmem_st_16x32bx2_x16<32>(tmem + lane_addr + Tr::kColS + h * 16, chunk);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) chunk[i] = pk_s[16 * h + i];
-        tmem_st_16x32bx2_x16<32>(tmem + lane_addr + Tr::kColDP + h * 16, chunk);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(smem_u32(p_full));
     }
     // ---- epilogue: dV = P^T dO, dK = scale * dS^T Q, in the input type.
     bool have = ok && n_steps > 0;
