@@ -87,10 +87,15 @@ struct BwdTraits {
   static constexpr int kTileBytes = kBlockM * D * 2;  // every tile is 128 rows x D
   static constexpr int kBoxBytes = kBlockM * 128;
   static constexpr int kNumBoxes = D / 64;
-  static constexpr int kStages = D == 128 ? 4 : 8;
-  // q_full, kv_full/empty[NS], s_full, s_free, ds_full[2], ds_free[2], acc_done, mma_drain
-  static constexpr int kNumBarriers = 1 + 2 * kStages + 8;
-  static constexpr int kSmemBytes = 1024 + (2 + kStages) * kTileBytes + kNumBarriers * 8 + 16;
+  // K and V have rings of their own: K_j stays in its slot until dQ += dS_j K_j
+  // has run (after block j's elementwise work), V_j only until dP_j, so K gets
+  // the deeper ring and its next load is not held up behind that late release.
+  static constexpr int kStagesK = D == 128 ? 3 : 5;
+  static constexpr int kStagesV = D == 128 ? 2 : 3;
+  // q_full, k_full/empty[NK], v_full/empty[NV], s_full, s_free, ds_full[2], ds_free[2], acc_done, mma_drain
+  static constexpr int kNumBarriers = 1 + 2 * (kStagesK + kStagesV) + 8;
+  static constexpr int kSmemBytes =
+      1024 + (2 + kStagesK + kStagesV) * kTileBytes + kNumBarriers * 8 + 16;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -116,18 +121,21 @@ __device__ __forceinline__ void ds_pack(const float (&s)[64], const float (&dp)[
 template <int D, bool kBf16, bool kCausal>
 __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_constant__ BwdKernelParams p) {
   using Tr = BwdTraits<D>;
-  constexpr int NS = Tr::kStages;
+  constexpr int NK = Tr::kStagesK;
+  constexpr int NV = Tr::kStagesV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;
   uint8_t* sDO = smem + Tr::kTileBytes;
-  uint8_t* sKV = smem + 2 * Tr::kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NS * Tr::kTileBytes);
+  uint8_t* sKV = smem + 2 * Tr::kTileBytes;  // K slots [0, NK), then V slots [NK, NK + NV)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + (NK + NV) * Tr::kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + NS;
-  uint64_t* s_full = kv_empty + NS;  // S and dP of the block are in TMEM
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + NK;
+  uint64_t* v_full = k_empty + NK;
+  uint64_t* v_empty = v_full + NV;
+  uint64_t* s_full = v_empty + NV;  // S and dP of the block are in TMEM
   uint64_t* s_free = s_full + 1;     // the elementwise warps hold S and dP in registers
   uint64_t* ds_full = s_free + 1;    // [2] dS of the buffer's block is in TMEM
   uint64_t* ds_free = ds_full + 2;   // [2] dQ += dS K of the buffer's last block is done
@@ -171,9 +179,13 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(smem_u32(&kv_full[i]), 1);
-      mbar_init(smem_u32(&kv_empty[i]), 1);
+    for (int i = 0; i < NK; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_empty[i]), 1);
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(smem_u32(&v_full[i]), 1);
+      mbar_init(smem_u32(&v_empty[i]), 1);
     }
     mbar_init(smem_u32(s_full), 1);
     mbar_init(smem_u32(s_free), 2 * kBlockM);
@@ -235,35 +247,42 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
                       pol_q);
         }
       }
-      int it = 0;
+      int loads[2] = {0, 0};  // K and V loads issued
       bool ok = true;
       for (int j = 0; j < n_blocks && ok; ++j) {
-        for (int kv = 0; kv < 2 && ok; ++kv, ++it) {  // K_j, then V_j
-          const int slot = it % NS;
-          const uint32_t fill = static_cast<uint32_t>(it / NS);
-          if (!wait_all(&kv_empty[slot], (fill & 1u) ^ 1u)) {
+        for (int kv = 0; kv < 2 && ok; ++kv) {  // K_j, then V_j
+          const int ns = kv == 0 ? NK : NV;
+          const int slot = j % ns;
+          const uint32_t fill = static_cast<uint32_t>(j / ns);
+          uint64_t* empty = kv == 0 ? &k_empty[slot] : &v_empty[slot];
+          if (!wait_all(empty, (fill & 1u) ^ 1u)) {
             ok = false;
             break;
           }
           if (leader) {
-            const uint32_t bar = smem_u32(&kv_full[slot]);
+            const uint32_t bar = smem_u32(kv == 0 ? &k_full[slot] : &v_full[slot]);
             mbar_arrive_expect_tx(bar, Tr::kTileBytes);
             const CUtensorMap* tm = kv == 0 ? &p.tm_k : &p.tm_v;
+            uint8_t* dst = sKV + (kv == 0 ? slot : NK + slot) * Tr::kTileBytes;
             for (int bx = 0; bx < Tr::kNumBoxes; ++bx) {
-              tma_load_4d(smem_u32(sKV + slot * Tr::kTileBytes + bx * Tr::kBoxBytes), tm, bar, bx * 64, kv_head,
-                          j * kBlockN, batch, pol_kv);
+              tma_load_4d(smem_u32(dst + bx * Tr::kBoxBytes), tm, bar, bx * 64, kv_head, j * kBlockN, batch, pol_kv);
             }
           }
+          ++loads[kv];
         }
       }
       if (!ok) {
+        // Error path: let every copy already issued land before the CTA exits
+        // (the last fill of each slot of both rings).
         const uint64_t drain_ns = 200ull * 1000 * 1000;
         int zero = 0;
         volatile int* never = &zero;
         mbar_wait(smem_u32(q_full), 0, never, drain_ns);
-        for (int s2 = 0; s2 < NS && s2 < it; ++s2) {
-          const int last = s2 + ((it - 1 - s2) / NS) * NS;
-          mbar_wait(smem_u32(&kv_full[s2]), static_cast<uint32_t>(last / NS) & 1u, never, drain_ns);
+        for (int j2 = loads[0] - NK > 0 ? loads[0] - NK : 0; j2 < loads[0]; ++j2) {
+          mbar_wait(smem_u32(&k_full[j2 % NK]), static_cast<uint32_t>(j2 / NK) & 1u, never, drain_ns);
+        }
+        for (int j2 = loads[1] - NV > 0 ? loads[1] - NV : 0; j2 < loads[1]; ++j2) {
+          mbar_wait(smem_u32(&v_full[j2 % NV]), static_cast<uint32_t>(j2 / NV) & 1u, never, drain_ns);
         }
       }
     } else if (warp == 9 && n_blocks > 0) {
@@ -306,22 +325,22 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
         __syncwarp();
       };
       bool ok = wait_all(q_full, 0);
-      int it = 0;
+      int jn = 0;  // next block whose S and dP are to be issued
       int kslot_cur = 0, kslot_next = 0;
-      // K_j and V_j in fill order; S and dP of block 0 first.
+      // S and dP of block jn (block 0 first).  issue_ss takes a slot index
+      // into the K slots followed by the V slots.
       auto issue_sdp = [&](int& kslot) {
-        kslot = it % NS;
-        bool r = wait_all(&kv_full[kslot], static_cast<uint32_t>(it / NS) & 1u);
-        ++it;
-        const int vslot = it % NS;
-        r = r && wait_all(&kv_full[vslot], static_cast<uint32_t>(it / NS) & 1u);
-        ++it;
+        kslot = jn % NK;
+        const int vslot = jn % NV;
+        bool r = wait_all(&k_full[kslot], static_cast<uint32_t>(jn / NK) & 1u);
+        r = r && wait_all(&v_full[vslot], static_cast<uint32_t>(jn / NV) & 1u);
+        ++jn;
         if (!r) return false;
         tc_fence_after();
-        issue_ss(kColS, desc_q, kslot);    // S = Q K_j^T
-        issue_ss(kColDP, desc_do, vslot);  // dP = dO V_j^T
+        issue_ss(kColS, desc_q, kslot);         // S = Q K_j^T
+        issue_ss(kColDP, desc_do, NK + vslot);  // dP = dO V_j^T
         commit(s_full);
-        commit(&kv_empty[vslot]);
+        commit(&v_empty[vslot]);
         return true;
       };
       if (ok && n_blocks > 0) {
@@ -341,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
         tc_fence_after();
         issue_dq(kslot_cur, kColDS + (j & 1) * 64, j > 0);  // dQ += dS_j K_j
         commit(&ds_free[j & 1]);
-        commit(&kv_empty[kslot_cur]);
+        commit(&k_empty[kslot_cur]);
         kslot_cur = kslot_next;
       }
       if (issued) {
