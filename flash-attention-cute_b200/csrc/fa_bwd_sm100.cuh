@@ -14,12 +14,17 @@
 //                           TMEM), the 8 elementwise warps form dS and write
 //                           it back to TMEM as 16-bit pairs, then
 //                           dQ += dS K (A read from TMEM, K as an MN-major
-//                           operand -- the forward's O += P V form);
+//                           operand -- the forward's O += P V form); K and V
+//                           stream through rings of their own, since K stays
+//                           in use until dQ's product and V only until dP's;
 //   * fa_bwd_dkdv_kernel    one 128-key tile per CTA (all query heads of its
-//                           K/V head under GQA): S^T = K Q^T and
-//                           dP^T = V dO^T with keys on the TMEM lanes, the
-//                           elementwise warps write P^T and dS^T as 16-bit
-//                           pairs, then dV += P^T dO and dK += dS^T Q.
+//                           K/V head under GQA), each step's 128 queries in
+//                           two halves of 64: S^T = K Q^T and dP^T = V dO^T
+//                           with keys on the TMEM lanes, the elementwise
+//                           warps write P^T and dS^T as 16-bit pairs, then
+//                           dV += P^T dO and dK += dS^T Q -- one half's
+//                           elementwise work overlapping the other half's
+//                           MMAs.
 // TMA tiles, swizzles, descriptors, bounded waits and the error flag are the
 // forward kernel's (fa_fwd_sm100.cuh / sm100_ptx.cuh).
 #pragma once
