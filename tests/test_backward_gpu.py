@@ -21,11 +21,18 @@ def _lowp_grads(q, k, v, do, causal, q_off):
     qd, kd, vd = (t.cuda().requires_grad_(True) for t in (q, k, v))
     kr, vr = kd.repeat_interleave(h // hk, dim=2), vd.repeat_interleave(h // hk, dim=2)
     s = torch.einsum("bqhd,bkhd->bhqk", qd, kr).float() / math.sqrt(q.shape[3])
+    dead = None
     if causal:
         i = torch.arange(q.shape[1], device="cuda")[:, None] + q_off
         j = torch.arange(k.shape[1], device="cuda")[None, :]
         s = s.masked_fill(j > i, float("-inf"))
-    p = torch.softmax(s, dim=-1).to(q.dtype)
+        # rows that see no key at all contribute nothing (P = 0), as in the kernels
+        dead = torch.isinf(s).all(dim=-1, keepdim=True)
+        s = s.masked_fill(dead, 0.0)
+    p = torch.softmax(s, dim=-1)
+    if dead is not None:
+        p = p.masked_fill(dead, 0.0)
+    p = p.to(q.dtype)
     o = torch.einsum("bhqk,bkhd->bqhd", p, vr)
     o.backward(do.cuda())
     return qd.grad.float().cpu(), kd.grad.float().cpu(), vd.grad.float().cpu()
@@ -47,6 +54,7 @@ def _check(grads, lowp, ref):
         (1, 384, 640, 8, 2, 128, torch.bfloat16, True),  # GQA, s_q < s_k, bottom-right causal
         (2, 129, 200, 2, 2, 128, torch.float16, False),  # tails
         (1, 1024, 1024, 2, 1, 64, torch.bfloat16, True),  # MQA
+        (1, 640, 384, 4, 2, 128, torch.bfloat16, True),  # s_q > s_k: the first 256 rows see no key
     ],
 )
 def test_backward_matches_fp32_autograd(b, sq, sk, h, hk, d, dtype, causal):
