@@ -106,7 +106,8 @@ struct BwdTraits {
 
 // P = exp2(s * c + neg) masked to the first `valid` entries, then
 // dS = P * (dP - dd), packed to 16-bit pairs.  (One 64-key half row.)
-template <bool kBf16>
+// kMask = false: the caller knows every entry is visible.
+template <bool kBf16, bool kMask>
 __device__ __forceinline__ void ds_pack(const float (&s)[64], const float (&dp)[64], float c, float neg, float dd,
                                         int64_t valid, uint32_t (&pk)[32]) {
   const float2 c2 = make_float2(c, c);
@@ -116,10 +117,33 @@ __device__ __forceinline__ void ds_pack(const float (&s)[64], const float (&dp)[
   for (int i = 0; i < 32; ++i) {
     const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), c2, n2);
     float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-    if (2 * i >= valid) pe.x = 0.f;
-    if (2 * i + 1 >= valid) pe.y = 0.f;
+    if (kMask) {
+      if (2 * i >= valid) pe.x = 0.f;
+      if (2 * i + 1 >= valid) pe.y = 0.f;
+    }
     const float2 g = __fmul2_rn(pe, __fadd2_rn(make_float2(dp[2 * i], dp[2 * i + 1]), make_float2(-d2.x, -d2.y)));
     pk[i] = pack2<kBf16>(g.x, g.y);
+  }
+}
+
+// The dK/dV kernel's elementwise step for one thread's 32 query columns of
+// a half: P^T = exp2(s * c + nl) with the first `lo` queries masked (kMask),
+// dS^T = P^T * (dP^T - dd), both packed to 16-bit pairs.
+template <bool kBf16, bool kMask>
+__device__ __forceinline__ void pds_pack(const float (&sv)[32], const float (&dpv)[32], float c, const float* nl,
+                                         const float* ddv, int64_t lo, uint32_t (&pk_p)[16], uint32_t (&pk_s)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), make_float2(c, c),
+                                make_float2(nl[2 * i], nl[2 * i + 1]));
+    float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+    if (kMask) {
+      if (2 * i < lo) pe.x = 0.f;
+      if (2 * i + 1 < lo) pe.y = 0.f;
+    }
+    const float2 g = __fmul2_rn(pe, make_float2(dpv[2 * i] - ddv[2 * i], dpv[2 * i + 1] - ddv[2 * i + 1]));
+    pk_p[i] = pack2<kBf16>(pe.x, pe.y);
+    pk_s[i] = pack2<kBf16>(g.x, g.y);
   }
 }
 
@@ -424,7 +448,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dq_kernel(const __grid_con
         valid = cl < valid ? cl : valid;
       }
       uint32_t pk[32];
-      ds_pack<kBf16>(sv, dpv, c, neg, dd, valid, pk);
+      if (__any_sync(0xffffffffu, valid < 64)) {
+        ds_pack<kBf16, true>(sv, dpv, c, neg, dd, valid, pk);
+      } else {
+        ds_pack<kBf16, false>(sv, dpv, c, neg, dd, valid, pk);
+      }
       // dS buffer j&1 is free once dQ += dS_{j-2} K_{j-2} has completed.
       if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(smem_u32(&ds_free[j & 1]),
                                                       static_cast<uint32_t>((j - 2) >> 1) & 1u, vabort, tmo))) {
@@ -809,16 +837,10 @@ __global__ void __launch_bounds__(kThreads, 1) fa_bwd_dkdv_kernel(const __grid_c
         const float* nl = stage_nl(slot) + 64 * hh + qh * 32;
         const float* ddv = stage_dd(slot) + 64 * hh + qh * 32;
         uint32_t pk_p[16], pk_s[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), make_float2(c, c),
-                                      make_float2(nl[2 * i], nl[2 * i + 1]));
-          float2 pe = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-          if (2 * i < lo) pe.x = 0.f;
-          if (2 * i + 1 < lo) pe.y = 0.f;
-          const float2 g = __fmul2_rn(pe, make_float2(dpv[2 * i] - ddv[2 * i], dpv[2 * i + 1] - ddv[2 * i + 1]));
-          pk_p[i] = pack2<kBf16>(pe.x, pe.y);
-          pk_s[i] = pack2<kBf16>(g.x, g.y);
+        if (__any_sync(0xffffffffu, lo > 0)) {
+          pds_pack<kBf16, true>(sv, dpv, c, nl, ddv, lo, pk_p, pk_s);
+        } else {
+          pds_pack<kBf16, false>(sv, dpv, c, nl, ddv, lo, pk_p, pk_s);
         }
         // P^T_hh over the first 32 columns of S^T_hh, dS^T_hh over those of dP^T_hh
         // (query q of the half in column q / 2)
