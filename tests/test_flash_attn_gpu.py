@@ -129,6 +129,20 @@ def test_bottom_right_causal(sq, sk):
     assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.float16]
 
 
+@pytest.mark.parametrize("sq,sk", [(700, 300), (513, 129)])
+def test_bottom_right_causal_more_queries_than_keys(sq, sk):
+    """Bottom-right causal with s_q > s_k: the first s_q - s_k query rows see
+    no key at all and come out as O = 0, LSE = -inf, like the oracle's."""
+    from flash_attention._C import forward_with_lse
+
+    q, k, v = make_inputs(1, sq, 2, 128, torch.bfloat16, seed=24, seqlen_k=sk)
+    o, lse = forward_with_lse(q.cuda(), k.cuda(), v.cuda(), True, q_pos_offset=sk - sq)
+    o_ref, lse_ref = math_attention(q, k, v, True, q_pos_offset=sk - sq)
+    assert (o.float().cpu() - o_ref).abs().max() <= O_TOL[torch.bfloat16]
+    assert _lse_err(lse, lse_ref) <= LSE_TOL
+    assert bool((o[:, : sq - sk].float() == 0).all()) and bool(torch.isneginf(lse[:, :, : sq - sk]).all())
+
+
 @pytest.mark.parametrize("dtype,causal", [(torch.bfloat16, False), (torch.float16, True)])
 def test_fp32_partials_merge_to_full_attention(dtype, causal):
     """fp32 partial outputs over disjoint key ranges (out_f32), combined by
